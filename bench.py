@@ -1,0 +1,429 @@
+"""Benchmark: InfLLM-v2 block selection at 128k prefill on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: one 131072-token sequence, q [131072, 32, 128]
+bf16 ~ N(0,1), compressed keys k_cmp [8191, 2, 128] bf16 ~ N(0,1), causal.
+One step is the whole path: stage 1 -> max_pooling_1d_varlen (block 64,
+stride 16, 1 init + 2 local blocks) -> top-64 -> get_block_table with a
+per-token block table [1, 131072] (a random permutation).  Inputs and
+outputs (q 1.07 GB, scores 4.3 GB, slots 4.3 GB) are far larger than the
+126 MB L2, so no explicit flush is needed between steps.
+
+Multi-GPU (torchrun, one process per GPU): every rank runs its own 128k
+sequence (independent units, no collective on the data path); the step time
+is the max over ranks, value = N * 131072 tokens / step time (weak scaling).
+
+--impl reference times the reference's CPU path on this host: the C
+restatement of the reference's torch/Triton semantics (oracle/, "port"),
+with all host threads, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L_SEQ = 131072
+HQ, HK, D = 32, 2, 128
+NKC = (L_SEQ - 32) // 16 + 1  # 8191 compressed keys
+TOPK = 64
+INIT_BLOCKS, LOCAL_BLOCKS = 1, 2
+METRIC = "block-selection tokens/s at 128k prefill (stage1+pool+topk+get_block_table)"
+
+
+def visible_counts(L=L_SEQ, k_len=NKC):
+    lq = np.arange(L, dtype=np.int64)
+    off = np.trunc((lq - 15) / 16).astype(np.int64) + k_len - (L - 15) // 16
+    return np.clip(off, 0, k_len)
+
+
+def stage1_flops():
+    """Algorithmic work of stage 1: one QK^T pass over the visible pairs."""
+    return float(2 * D * HQ * visible_counts().sum())
+
+
+def algorithmic_bytes():
+    """Per-kernel algorithmic HBM bytes of one step (bf16 scores, int32 ids)."""
+    W = (NKC + 127) // 128 * 128
+    NB = (L_SEQ + 63) // 64
+    T = L_SEQ
+    return {
+        "pool": HK * T * W * 2 + HK * T * NB * 2,
+        "topk": HK * T * NB * 2 + HK * T * TOPK * 4,
+        "get_block_table": T * HK * TOPK * 64 * 4 + HK * T * TOPK * 4 + 8 * T + 4 * L_SEQ,
+        "stage1_out": HK * T * W * 2,
+    }
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), d.get(
+            "bf16_tflops_sustained", 1400.0), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of each kernel from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "traffic_c3.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{index}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index),
+                 "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.fh,
+                stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": smax, "reasons": sorted(reasons)}
+        loaded = sorted(sm)[len(sm) // 4:] or sm  # drop idle samples at the edges
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_inputs(seed, device):
+    import torch
+
+    gdev = device if device is not None else "cpu"
+    g = torch.Generator(device=gdev).manual_seed(seed)
+    q = torch.randn(L_SEQ, HQ, D, generator=g, dtype=torch.float32, device=gdev).to(torch.bfloat16)
+    k = torch.randn(NKC, HK, D, generator=g, dtype=torch.float32, device=gdev).to(torch.bfloat16)
+    table = torch.randperm(L_SEQ, generator=g, dtype=torch.int64, device=gdev).to(
+        torch.int32).reshape(1, L_SEQ)
+    q, k, table = q.cpu(), k.cpu(), table.cpu()
+    cu_q = torch.tensor([0, L_SEQ], dtype=torch.int32)
+    cu_k = torch.tensor([0, NKC], dtype=torch.int32)
+    tb = torch.zeros(L_SEQ, dtype=torch.int32)
+    pos = torch.arange(1, L_SEQ + 1, dtype=torch.int32)
+    seqlen = torch.tensor([L_SEQ], dtype=torch.int32)
+    host = dict(q=q, k=k, table=table, cu_q=cu_q, cu_k=cu_k, tb=tb, pos=pos, seqlen=seqlen)
+    return host
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import unum_ops_b200
+    from unum_ops_b200 import block_select
+    from unum_ops_b200.infllm_v2 import (infllmv2_attn_stage1, max_pooling_1d_varlen,
+                                         stage1_status)
+    from unum_ops_b200.sparse_kernel_extension import get_block_table_ref_torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    unum_ops_b200.load()
+
+    host = make_inputs(1234 + 3 + rank, dev)
+    d = {k: v.to(dev) for k, v in host.items()}
+    stream = torch.cuda.current_stream(dev)
+    W = (NKC + 127) // 128 * 128
+    zeros_cache = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def step(ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        scores = infllmv2_attn_stage1(d["q"], d["k"], None, d["cu_q"], d["cu_k"], max_seqlen_k=NKC,
+                                      causal=True)
+        if ev is not None:
+            ev[1].record(stream)
+        pooled = max_pooling_1d_varlen(scores, d["cu_q"], d["cu_k"], zeros_cache, 16 * W, L_SEQ,
+                                       LOCAL_BLOCKS, INIT_BLOCKS)
+        if ev is not None:
+            ev[2].record(stream)
+        idx = unum_ops_b200.topk_blocks(pooled, TOPK)
+        if ev is not None:
+            ev[3].record(stream)
+        slots = get_block_table_ref_torch(idx, d["table"], d["tb"], d["pos"], d["seqlen"])
+        if ev is not None:
+            ev[4].record(stream)
+        return scores, pooled, idx, slots
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        out = step()
+    barrier()
+    if stage1_status(dev) != 0:
+        raise RuntimeError("stage-1 kernel reported a timeout")
+    del out
+
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        t_start.record(stream)
+        for i in range(args.steps):
+            out = step(evs[i])
+        t_end.record(stream)
+        barrier()
+    total_ms = t_start.elapsed_time(t_end)
+    per = {"stage1": [], "pool": [], "topk": [], "get_block_table": []}
+    for e in evs:
+        per["stage1"].append(e[0].elapsed_time(e[1]))
+        per["pool"].append(e[1].elapsed_time(e[2]))
+        per["topk"].append(e[2].elapsed_time(e[3]))
+        per["get_block_table"].append(e[3].elapsed_time(e[4]))
+    ms_step = total_ms / args.steps
+    if world > 1:
+        t = torch.tensor([ms_step], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_step = float(t.item())
+    del out
+
+    # ---- end to end through the public API with host buffers (pinned), copies timed
+    pin = {k: v.pin_memory() for k, v in host.items()}
+    res_host = torch.empty(HK, L_SEQ, TOPK, dtype=torch.int32).pin_memory()
+
+    def e2e_step():
+        dd = {k: v.to(dev, non_blocking=True) for k, v in pin.items()}
+        _, _, idx, slots = block_select(dd["q"], dd["k"], dd["cu_q"], dd["cu_k"], NKC, dd["table"],
+                                        dd["tb"], dd["pos"], dd["seqlen"], max_context_len=L_SEQ,
+                                        init_blocks=INIT_BLOCKS, local_blocks=LOCAL_BLOCKS,
+                                        topk=TOPK)
+        res_host.copy_(idx, non_blocking=True)
+        return slots
+
+    e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(1, min(args.steps, 5))
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    h2d = sum(v.numel() * v.element_size() for v in pin.values())
+    d2h = res_host.numel() * 4
+
+    if rank == 0:
+        hbm, tf_burst, tf_sus, src = load_peaks()
+        mean = {k: statistics.mean(v) for k, v in per.items()}
+        flops = stage1_flops()
+        ab = algorithmic_bytes()
+        traffic = load_traffic()
+        s1_tf = flops / (mean["stage1"] * 1e-3) / 1e12
+        kernels = {
+            "stage1": {"ms": mean["stage1"], "tflops": s1_tf, "frac": s1_tf / tf_sus,
+                       "bound": "tensor",
+                       "out_gbs": ab["stage1_out"] / (mean["stage1"] * 1e-3) / 1e9},
+        }
+        for kname in ("pool", "topk", "get_block_table"):
+            gbs = ab[kname] / (mean[kname] * 1e-3) / 1e9
+            kernels[kname] = {"ms": mean[kname], "gbs": gbs, "frac": gbs / hbm, "bound": "hbm"}
+        cpu = None
+        if args.cpu_sample > 0:
+            hf = {k: v.numpy() for k, v in host.items() if k not in ("q", "k")}
+            hf["q"] = host["q"].float().numpy()
+            hf["k"] = host["k"].float().numpy()
+            cpu = cpu_baseline(args, sample_tokens=args.cpu_sample, host=hf)
+        line = {
+            "metric": METRIC,
+            "value": world * L_SEQ / (ms_step * 1e-3),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_step,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) q/k_cmp, random-permutation block table)",
+            "config": {"workload": "C3: 128k-token causal prefill, 32 q-heads / 2 kv-heads, d=128, "
+                                   "k_cmp 8191, NB 2048, top-64, per-token block table [1,131072]",
+                       "tokens_per_gpu": L_SEQ, "parallelism": f"dp{world} (one sequence per GPU)",
+                       "l2": "inputs larger than L2 (q 1.07 GB, scores 4.3 GB, slots 4.3 GB)"},
+            "roofline": {"bound": "tensor", "kernel": "stage1", "achieved": s1_tf,
+                         "peak": tf_sus, "unit": "TFLOP/s", "frac": s1_tf / tf_sus,
+                         "peak_source": f"{src} bf16_tflops_sustained",
+                         "algorithmic": "2*D*Hq*sum_t visible(t) = %.4g flop per launch" % flops,
+                         "traffic": traffic.get("stage1")},
+            "kernels": kernels,
+            "e2e": {"value": world * L_SEQ / (e2e_ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                    "result": "top-64 block ids int32 [2,131072,64] copied to host"},
+            "gpu_launches": 5 * args.steps,
+            "clocks": clk.summary(),
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ CPU baseline
+def cpu_baseline(args, sample_tokens=2048, repeats=1, host=None):
+    """Time the reference's semantics on the host (C port in oracle/, all threads)
+    on `sample_tokens` consecutive tokens in the middle of the 128k sequence;
+    scale to tokens/s by visible-pair count (stage 1) and token count (rest)."""
+    import oracle
+
+    nthreads = oracle.set_num_threads(0)
+    if host is None:
+        host = host_inputs_f32()
+    q = host["q"]
+    k = host["k"]
+    cu_q = host["cu_q"]
+    cu_k = host["cu_k"]
+    vis = visible_counts()
+    a = L_SEQ // 2 - sample_tokens // 2
+    b = a + sample_tokens
+    W = (NKC + 127) // 128 * 128
+    NB = L_SEQ // 64
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        sc = oracle.stage1(q, k, cu_q, cu_k, True, t_range=(a, b))
+        t1 = time.perf_counter()
+        # downstream steps on the sampled rows only
+        cu_qs = np.array([-a, b - a], np.int32)  # sampled rows keep their positions
+        pooled = oracle.max_pool(sc, cu_qs, cu_k, np.zeros(1, np.int32), 16 * W, L_SEQ,
+                                 LOCAL_BLOCKS, INIT_BLOCKS)
+        t2 = time.perf_counter()
+        idx = oracle.topk(pooled, TOPK)
+        t3 = time.perf_counter()
+        oracle.get_block_table(idx, host["table"], host["tb"][a:b], host["pos"][a:b],
+                               host["seqlen"])
+        t4 = time.perf_counter()
+        frac_s1 = vis[a:b].sum() / vis.sum()
+        frac_rest = (b - a) / L_SEQ
+        full_s = (t1 - t0) / frac_s1 + (t4 - t1) / frac_rest
+        times.append((full_s, t1 - t0, t4 - t1))
+    full_s = statistics.median(t[0] for t in times)
+    return {"value": L_SEQ / full_s, "unit": "tokens/s", "cores": nthreads, "kind": "port",
+            "sample": f"tokens [{a},{b}) of the 128k sequence (stage1 scaled by visible pairs "
+                      f"{vis[a:b].sum() / vis.sum():.4f} of total, pool/topk/get_block_table by "
+                      f"token count); extrapolated full step {full_s:.1f} s"}
+
+
+def host_inputs_f32():
+    host = make_inputs(1234 + 3, None)
+    out = {k: v.numpy() for k, v in host.items() if k not in ("q", "k")}
+    out["q"] = host["q"].float().numpy()
+    out["k"] = host["k"].float().numpy()
+    return out
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    host = host_inputs_f32()
+    steps = []
+    for i in range(args.warmup + args.steps):
+        cb = cpu_baseline(args, sample_tokens=args.ref_sample, host=host)
+        if i >= args.warmup:
+            steps.append(cb)
+    vals = [s["value"] for s in steps]
+    v = statistics.median(vals)
+    line = {
+        "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": L_SEQ / v * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "reference",
+        "data": "synthetic (seeded N(0,1) q/k_cmp, random-permutation block table)",
+        "config": {"workload": "C3: 128k-token causal prefill, 32 q-heads / 2 kv-heads, d=128, "
+                               "k_cmp 8191, NB 2048, top-64, per-token block table [1,131072]",
+                   "host": "CPU reference path (C port of the reference semantics, oracle/)"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": steps[0]["cores"],
+                         "kind": "port", "sample": steps[0]["sample"]},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-sample", type=int, default=8192,
+                    help="tokens of the CPU-baseline sample (0: skip)")
+    ap.add_argument("--ref-sample", type=int, default=2048)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,157 @@
+/*
+ * unum_ops_b200 — C ABI of the B200 (sm_100a) InfLLM-v2 block-selection path.
+ *
+ * Every entry point takes raw device pointers, element counts and strides and
+ * a CUDA stream (as `void *`, i.e. a cudaStream_t; NULL = legacy default
+ * stream), enqueues its kernels on that stream and returns without
+ * synchronising.  Return value: 0 on success, a negative UNUM_ERR_* code on
+ * failure, with a message available from unum_last_error() (thread-local).
+ * No C++ exception crosses this boundary, no entry point allocates device
+ * memory, and all outputs are fully written by the kernels (callers may pass
+ * uninitialised buffers).
+ *
+ * Reference interfaces replaced (Yanguan619/unum_ops, Python):
+ *   unum_infllmv2_attn_stage1   <- src/unum_ops/infllm_v2/infllmv2_attn_stage1_triton_v2.py:170-245
+ *                                  (public alias infllm_v2/__init__.py:3-5)
+ *   unum_max_pooling_1d_varlen  <- src/unum_ops/infllm_v2/max_pooling_1d_varlen.py:127-183
+ *                                  (public alias infllm_v2/__init__.py:7-9)
+ *   unum_get_block_table        <- src/unum_ops/sparse_kernel_extension/get_table_torch.py:4-44
+ *                                  and get_table_triton.py:218-369 (aliases __init__.py:1-12)
+ *   unum_topk_blocks            <- no reference function: the reference's caller runs torch.topk
+ *                                  on the pooled scores; the selection rule is stated below.
+ */
+#ifndef UNUM_OPS_B200_H
+#define UNUM_OPS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define UNUM_OK 0
+#define UNUM_ERR_INVALID (-1)     /* bad argument (shape, size, alignment, null pointer) */
+#define UNUM_ERR_UNSUPPORTED (-2) /* valid but not implemented on this path (e.g. head_dim != 128) */
+#define UNUM_ERR_CUDA (-3)        /* a CUDA runtime/driver call failed */
+#define UNUM_ERR_WORKSPACE (-4)   /* workspace missing or too small */
+
+/* Element types of score tensors. */
+#define UNUM_DTYPE_F32 0
+#define UNUM_DTYPE_BF16 1
+#define UNUM_DTYPE_F16 2
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char *unum_last_error(void);
+
+/* ABI version of this library (major * 100 + minor). */
+int unum_abi_version(void);
+
+/*
+ * get_block_table — logical top-k blocks to physical KV slot ids.
+ * Replaces get_block_table_ref_torch (get_table_torch.py:4-44) and the Triton
+ * variants get_block_table_ref_triton{,_v2,_v3} (get_table_triton.py:218-369).
+ *
+ *   topk_idx       int32 [H, T, K], element strides (ts_h, ts_t, ts_k)
+ *   block_table    int32 [B, L], row stride bt_stride (elements), column stride 1
+ *   token_to_bs    int32 [T]
+ *   token_pos_in_bs int32 [T], or one value broadcast when pos_is_scalar != 0
+ *   seqlen_q       int32 [B], or one value broadcast when seqlen_is_scalar != 0
+ *   out            int32 [T, H, K*64] contiguous, fully written
+ *
+ *   out[t,h,k*64+i] = head_group * block_table[bs, clamp(pos, 0, L-1)] + h
+ *       if pos >= 0 && pos < seqlen_q[bs] && pos < token_pos_in_bs[t], else 0,
+ *   with pos = topk_idx[h,t,k]*64 + i, bs = token_to_bs[t], int32 wrap-around.
+ * head_group is 2 in the torch reference (get_table_torch.py:12) and H in the
+ * Triton kernels (get_table_triton.py:252).  token_to_bs values must lie in
+ * [0, B); the kernel checks and writes 0 for a token outside that range.
+ */
+int unum_get_block_table(const int32_t *topk_idx, int64_t H, int64_t T, int64_t K,
+                         int64_t ts_h, int64_t ts_t, int64_t ts_k,
+                         const int32_t *block_table, int64_t B, int64_t L, int64_t bt_stride,
+                         const int32_t *token_to_bs, const int32_t *token_pos_in_bs,
+                         int pos_is_scalar, const int32_t *seqlen_q, int seqlen_is_scalar,
+                         int32_t head_group, int32_t *out, void *stream);
+
+/*
+ * max_pooling_1d_varlen — compressed scores to 64-token-block scores.
+ * Replaces max_pooling_1d_varlen_ref_triton (max_pooling_1d_varlen.py:127-183).
+ *
+ *   input   dtype [H, T, *] read as the flat buffer in[h*T*fs + t*fs + c] with
+ *           fs = max_seqlen_q / stride (the reference's flat_stride, :146);
+ *           input_numel bounds every read (an element past it counts as
+ *           masked — the reference reads out of bounds there).
+ *   cu_seqlens_q/k int32 [n_seq+1], cache_lens int32 [n_seq]
+ *   out     dtype [H, T, NB] contiguous, NB = ceil(max_context_len / block_size)
+ *
+ *   window of block j: c in [j*sp - 1, j*sp - 1 + sp + 1), sp = block_size/stride,
+ *   clipped to [0, k_len) with k_len = cu_k[b+1]-cu_k[b]+cache_lens[b];
+ *   out = +inf if j < init_blocks or j <= (t-cu_q[b])/block_size <= j+local_blocks,
+ *   else the window max, or -inf for an empty window.  NaN inputs are ignored.
+ */
+int unum_max_pooling_1d_varlen(const void *input, int dtype, int64_t H, int64_t T,
+                               int64_t input_numel, const int32_t *cu_seqlens_q,
+                               const int32_t *cu_seqlens_k, const int32_t *cache_lens,
+                               int64_t n_seq, int64_t max_seqlen_q, int64_t max_context_len,
+                               int64_t local_blocks, int64_t init_blocks, int64_t block_size,
+                               int64_t stride, void *out, void *stream);
+
+/*
+ * topk_blocks — top-K block selection per row of pooled scores.
+ * No reference counterpart (the reference's caller uses torch.topk).
+ *
+ *   scores dtype [rows, NB] with row stride row_stride (elements)
+ *   out    int32 [rows, K] contiguous
+ *
+ * Candidates are the entries that are neither -inf nor NaN; they are ranked by
+ * (score descending, block index ascending); the first min(K, #candidates)
+ * are written in ASCENDING block-index order, followed by -1 padding.
+ * Supports NB <= 4096 and K <= 1024.
+ */
+int unum_topk_blocks(const void *scores, int dtype, int64_t rows, int64_t NB,
+                     int64_t row_stride, int64_t K, int32_t *out, void *stream);
+
+/*
+ * infllmv2_attn_stage1 — compressed-key GQA scores, softmax per head, summed
+ * over each head group.  Replaces infllmv2_attn_stage1_triton_v2
+ * (infllmv2_attn_stage1_triton_v2.py:170-245; kernel :36-167).
+ *
+ *   q    bf16 [T, Hq, D], strides (q_st, q_sh) elements for t and head, d contiguous
+ *   k    bf16 [Tk, Hk, D], strides (k_st, k_sh), d contiguous
+ *   cu_seqlens_q/k int32 [n_seq+1] (device)
+ *   out  bf16 [Hk, T, out_stride] contiguous, fully written; out_stride is
+ *        the reference's round-up-128 of max_seqlen_k.
+ *
+ *   out[g,t,j] = sum over the G = Hq/Hk heads h of group g of
+ *                softmax_j(q[t,h] . k[k_start+j, g] * softmax_scale)
+ *   over the keys j visible to t, 0 elsewhere (also 0 for a token whose
+ *   softmax is empty, where the reference maps NaN to 0).  With causal != 0,
+ *   key j is visible iff j < clamp((lq-15)/16 + k_len - (q_len-15)/16, 0, k_len)
+ *   (C integer division, lq = t - cu_q[b]).
+ *
+ * Requirements: D == 128; G a power of two <= 256; q, k 16-byte aligned with
+ * 16-byte-multiple strides.  workspace: device memory of at least
+ * unum_stage1_workspace_size(n_seq) bytes, 16-byte aligned; its contents on
+ * entry do not matter.  Calls sharing a workspace must be stream-ordered.
+ */
+size_t unum_stage1_workspace_size(int64_t n_seq);
+
+int unum_infllmv2_attn_stage1(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st,
+                              int64_t q_sh, const void *k, int64_t Tk, int64_t Hk, int64_t k_st,
+                              int64_t k_sh, const int32_t *cu_seqlens_q,
+                              const int32_t *cu_seqlens_k, int64_t n_seq, float softmax_scale,
+                              int causal, void *out, int64_t out_stride, void *workspace,
+                              size_t workspace_bytes, void *stream);
+
+/*
+ * Status word a stage-1 launch leaves in its workspace: 0 = ok; nonzero = a
+ * bounded wait inside the kernel gave up (the output is then invalid).  Reads
+ * the word with a stream-ordered copy and synchronises the stream.
+ */
+int unum_stage1_status(const void *workspace, void *stream, int32_t *status_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* UNUM_OPS_B200_H */

@@ -90,7 +90,7 @@ def stage1(q, k, cu_q, cu_k, causal, scale=None, out_stride=None, t_range=None):
     q: [T, Hq, D], k: [Tk, Hk, D] (float32 values; bf16 inputs widened).
     out_stride defaults to round-up-128 of the longest compressed sequence,
     like infllmv2_attn_stage1_triton_v2.py:199-211.  t_range=(a, b) computes
-    only rows a..b-1 (other rows stay 0).
+    only the rows of tokens a..b-1 and returns [Hk, b-a, out_stride].
     """
     q = _c(q, np.float32)
     k = _c(k, np.float32)
@@ -104,10 +104,10 @@ def stage1(q, k, cu_q, cu_k, causal, scale=None, out_stride=None, t_range=None):
     if out_stride is None:
         mk = int(np.max(cu_k[1:] - cu_k[:-1])) if n_seq > 0 else 0
         out_stride = (mk + 127) // 128 * 128 if mk > 0 else 0
-    out = np.zeros((Hk, T, out_stride), np.float32)
-    if out_stride == 0 or T == 0:
+    a, b = (0, T) if t_range is None else (max(0, t_range[0]), min(T, t_range[1]))
+    out = np.zeros((Hk, max(0, b - a), out_stride), np.float32)
+    if out_stride == 0 or b <= a:
         return out
-    a, b = (0, T) if t_range is None else t_range
     lib().oracle_stage1(_p(q), _p(k), T, Hq, Hk, D, _p(cu_q), _p(cu_k), n_seq, float(scale),
                         int(bool(causal)), out_stride, a, b, _p(out))
     return out

@@ -112,9 +112,9 @@ int64_t oracle_stage1_visible(int64_t local_q, int64_t q_len, int64_t k_len, int
 /* :170-245 (wrapper).                                                      */
 /*   q   : [T, Hq, D]  values of the bf16 input, widened to float           */
 /*   k   : [Tk, Hk, D] values of the bf16 input, widened to float           */
-/*   out : [Hk, T, out_stride] float; rows t in [t_begin, t_end) are fully  */
-/*         written (zeros where the reference leaves its torch.zeros fill   */
-/*         or maps NaN to 0).                                                */
+/*   out : [Hk, t_end - t_begin, out_stride] float: the rows of tokens      */
+/*         t_begin..t_end-1, fully written (zeros where the reference       */
+/*         leaves its torch.zeros fill or maps NaN to 0).                    */
 /* Per (kv head g, token t): scores s_hj = (q_h . k_j) * scale for the      */
 /* visible keys j, softmax per head h of the group, then the sum over the   */
 /* group's heads (:160-161).  Invisible keys and keys past k_len give 0.     */
@@ -135,7 +135,7 @@ static void stage1_rows(int64_t rb, int64_t re, void *vctx) {
     int64_t s_cap = 0;
     for (int64_t r = rb; r < re; ++r) {
         int64_t g = r / c->nt, t = c->t_begin + r % c->nt;
-        float *orow = c->out + (g * c->T + t) * c->out_stride;
+        float *orow = c->out + (g * c->nt + (t - c->t_begin)) * c->out_stride;
         memset(orow, 0, sizeof(float) * (size_t)c->out_stride);
         int b = find_seq(c->cu_q, c->n_seq, t);
         if (b < 0) continue;

@@ -1,0 +1,15 @@
+"""unum_ops_b200: B200-native (sm_100a) InfLLM-v2 block selection.
+
+Drop-in for the hot path of Yanguan619/unum_ops:
+  unum_ops_b200.infllm_v2               <- unum_ops.infllm_v2
+  unum_ops_b200.sparse_kernel_extension <- unum_ops.sparse_kernel_extension
+plus unum_ops_b200.block_select (top-k and the chained pipeline).
+Kernels live in libunum_ops_b200.so (C ABI: include/unum_ops_b200.h).
+"""
+from . import infllm_v2, sparse_kernel_extension  # noqa: F401
+from .block_select import block_select, topk_blocks  # noqa: F401
+from ._build import build  # noqa: F401
+from ._lib import library_path, load  # noqa: F401
+
+__all__ = ["infllm_v2", "sparse_kernel_extension", "block_select", "topk_blocks", "build",
+           "load", "library_path"]

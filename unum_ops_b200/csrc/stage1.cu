@@ -1,0 +1,607 @@
+// infllmv2_attn_stage1 on B200: tcgen05 (TMEM) tensor-core kernel.
+//
+// Semantics follow the public Triton kernel of the reference
+// (src/unum_ops/infllm_v2/infllmv2_attn_stage1_triton_v2.py:36-167, wrapper
+// :170-245): for kv head g and token t,
+//     out[g,t,j] = sum_{h in group g} softmax_j(q[t,h] . k[k_start+j,g] * scale)
+// over the keys visible to t (causal rule :86-91), 0 elsewhere and 0 for an
+// empty softmax (the reference's NaN -> 0, :244).
+//
+// Work decomposition.  A tile is QT = 256/G consecutive tokens of one sequence
+// and one kv head: its 256 (token, head) rows of Q (64 KB bf16, loaded once by
+// TMA) meet the sequence's compressed keys in 128-key tiles.  Two passes over
+// the key tiles:
+//   pass 1  S = Q K^T        (2 x UMMA 128x128x128, rows = (token, head)):
+//           each epilogue thread owns one row and keeps its running max and
+//           sum of exp2 — the per-head softmax statistics;
+//   pass 2  S^T = K Q^T      (UMMA 128x256x128, rows = keys): each epilogue
+//           thread owns one key and sums exp2(s*c - b[row]) over the G heads
+//           of every token inside its own registers, so the head-group
+//           reduction needs no shuffles and the per-head probabilities never
+//           leave the SM.  Results go straight to HBM as bf16.
+// The same Q/K shared-memory tiles serve both passes (operand roles swap).
+//
+// Warp roles (320 threads, one CTA per SM, persistent over tiles):
+//   warps 0-7  epilogue (TMEM -> registers -> softmax math -> global)
+//   warp 8     TMA producer (Q tile, 4-stage ring of K tiles)
+//   warp 9     TMEM allocator + single-thread UMMA issuer
+// TMEM holds two 256-column accumulator buffers so the tensor core fills one
+// while the epilogue drains the other.
+//
+// Every wait on an mbarrier is bounded (about one second of globaltimer);
+// on expiry the kernel records a nonzero status word in the workspace, stops
+// issuing TMA/UMMA work, runs its remaining loops without waiting, frees TMEM
+// and returns, so the context stays usable and the host sees the status.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace {
+
+using namespace unum::sm100;
+
+constexpr int kD = 128;            // head dim
+constexpr int kRows = 256;         // (token, head) rows per tile
+constexpr int kBN = 128;           // keys per key tile
+constexpr int kStages = 4;         // K ring depth
+constexpr int kEpiWarps = 8;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kThreads = 320;
+constexpr uint32_t kTmemCols = 512;
+constexpr int kEpiBarrier = 1;     // named barrier id for the 256 epilogue threads
+
+constexpr uint32_t kQPanel = kRows * 128;          // one 64-column panel of Q: 32 KB
+constexpr uint32_t kQBytes = 2 * kQPanel;          // 64 KB
+constexpr uint32_t kKPanel = kBN * 128;            // 16 KB
+constexpr uint32_t kKStage = 2 * kKPanel;          // 32 KB
+constexpr uint32_t kOffK = kQBytes;
+constexpr uint32_t kOffStats = kOffK + kStages * kKStage;
+constexpr uint32_t kOffLim = kOffStats + kRows * 4;
+constexpr uint32_t kOffBar = kOffLim + kRows * 4;
+constexpr uint32_t kNumBars = 2 + 2 * kStages + 4;
+constexpr uint32_t kOffMisc = kOffBar + kNumBars * 8;
+constexpr uint32_t kSmemBytes = kOffMisc + 64 + 1024;  // + slack for 1024-byte alignment
+
+constexpr uint32_t kIdescP1 = idesc_bf16_f32(128, 128);
+constexpr uint32_t kIdescP2 = idesc_bf16_f32(128, 256);
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr uint64_t kWaitNs = 1000000000ull;  // bounded wait: 1 s
+
+// workspace layout (int32 words): [0] status, [1..3] reserved, [4..4+n_seq] tile prefix
+constexpr int kWsTiles = 4;
+
+struct Params {
+    const int32_t *cu_q;
+    const int32_t *cu_k;
+    int32_t *ws;
+    __nv_bfloat16 *out;
+    int64_t T;
+    int64_t out_stride;
+    int32_t n_seq;
+    int32_t Hk;
+    int32_t causal;
+    float c;  // softmax_scale * log2(e)
+};
+
+struct Item {
+    int32_t g;
+    int32_t nq;        // valid tokens in this tile
+    int32_t nkt;       // key tiles to compute
+    int32_t local0;    // position of the tile's first token inside its sequence
+    int32_t q_len, k_len;
+    int64_t t0, k_start;
+};
+
+// Visible compressed keys of a token (C integer division, like Triton's //).
+__device__ __forceinline__ int32_t visible(int32_t lq, int32_t q_len, int32_t k_len, int causal) {
+    if (k_len <= 0) return 0;
+    if (!causal) return k_len;
+    int32_t off = (lq - 15) / 16 + k_len - (q_len - 16 + 1) / 16;
+    return off < 0 ? 0 : (off > k_len ? k_len : off);
+}
+
+template <int QT>
+__device__ __forceinline__ Item decode(int64_t w, const Params &p, const int32_t *cu_tiles,
+                                       int32_t n_tiles) {
+    Item it;
+    it.g = (int32_t)(w % p.Hk);
+    const int32_t tile = n_tiles - 1 - (int32_t)(w / p.Hk);  // last tiles (longest rows) first
+    int32_t lo = 0, hi = p.n_seq;  // largest b with cu_tiles[b] <= tile
+    while (hi - lo > 1) {
+        const int32_t mid = (lo + hi) >> 1;
+        if (cu_tiles[mid] <= tile) lo = mid; else hi = mid;
+    }
+    const int32_t b = lo;
+    const int32_t chunk = tile - cu_tiles[b];
+    const int32_t qs = __ldg(p.cu_q + b);
+    it.q_len = __ldg(p.cu_q + b + 1) - qs;
+    it.local0 = chunk * QT;
+    it.t0 = (int64_t)qs + it.local0;
+    const int32_t rest = it.q_len - it.local0;
+    it.nq = rest < QT ? rest : QT;
+    it.k_start = __ldg(p.cu_k + b);
+    it.k_len = __ldg(p.cu_k + b + 1) - (int32_t)it.k_start;
+    const int32_t lim = visible(it.local0 + it.nq - 1, it.q_len, it.k_len, p.causal);
+    it.nkt = (lim + kBN - 1) / kBN;
+    return it;
+}
+
+struct Sync {
+    uint32_t q_full, q_empty, k_full, k_empty, s_full, s_empty;  // base addresses
+    volatile int *abort;
+    int32_t *status;
+};
+
+// Bounded wait: false once this CTA has given up (then callers stop issuing work).
+__device__ __forceinline__ bool wait_bar(const Sync &s, uint32_t bar, uint32_t parity, int code) {
+    if (*s.abort) return false;
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t_start = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 63) == 0) {
+            if (*s.abort) return false;
+            if (globaltimer_ns() - t_start > kWaitNs) {
+                *s.abort = 1;
+                atomicCAS(s.status, 0, code);
+                return false;
+            }
+        }
+    }
+}
+
+template <int G>
+__global__ void __launch_bounds__(kThreads, 1)
+stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+              const Params p) {
+    constexpr int QT = kRows / G;  // tokens per tile
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t sbase = (raw + 1023u) & ~1023u;
+    uint8_t *sgen = smem_raw + (sbase - raw);
+
+    float *stats = reinterpret_cast<float *>(sgen + kOffStats);
+    int32_t *lim_s = reinterpret_cast<int32_t *>(sgen + kOffLim);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(sgen + kOffMisc);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sgen + kOffMisc + 16);
+
+    Sync sy;
+    sy.q_full = sbase + kOffBar;
+    sy.q_empty = sy.q_full + 8;
+    sy.k_full = sy.q_full + 16;
+    sy.k_empty = sy.k_full + 8 * kStages;
+    sy.s_full = sy.k_empty + 8 * kStages;
+    sy.s_empty = sy.s_full + 16;
+    sy.abort = abort_flag;
+    sy.status = p.ws;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        mbar_init(sy.q_full, 1);
+        mbar_init(sy.q_empty, 1);
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(sy.k_full + 8 * s, 1);
+            mbar_init(sy.k_empty + 8 * s, 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(sy.s_full + 8 * b, 1);
+            mbar_init(sy.s_empty + 8 * b, kEpiWarps);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == kProducerWarp && lane == 0) {
+        prefetch_tmap(&tmQ);
+        prefetch_tmap(&tmK);
+    }
+    if (warp == kMmaWarp) {
+        tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    const int32_t *cu_tiles = p.ws + kWsTiles;
+    const int32_t n_tiles = cu_tiles[p.n_seq];
+    const int64_t n_items = (int64_t)n_tiles * p.Hk;
+
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            uint32_t kc = 0, qn = 0;
+            for (int64_t w = blockIdx.x; w < n_items; w += gridDim.x) {
+                const Item it = decode<QT>(w, p, cu_tiles, n_tiles);
+                if (it.nkt == 0) continue;
+                if (wait_bar(sy, sy.q_empty, (qn & 1) ^ 1, 1)) {
+                    mbar_arrive_expect_tx(sy.q_full, kQBytes);
+                    tma_load_3d(sbase, &tmQ, 0, it.g * G, (int32_t)it.t0, sy.q_full);
+                    tma_load_3d(sbase + kQPanel, &tmQ, 64, it.g * G, (int32_t)it.t0, sy.q_full);
+                }
+                ++qn;
+                for (int pass = 0; pass < 2; ++pass) {
+                    for (int32_t kt = 0; kt < it.nkt; ++kt, ++kc) {
+                        const uint32_t s = kc % kStages, ph = (kc / kStages) & 1;
+                        if (!wait_bar(sy, sy.k_empty + 8 * s, ph ^ 1, 2)) continue;
+                        const uint32_t dst = sbase + kOffK + s * kKStage;
+                        const int32_t krow = (int32_t)(it.k_start + (int64_t)kt * kBN);
+                        mbar_arrive_expect_tx(sy.k_full + 8 * s, kKStage);
+                        tma_load_3d(dst, &tmK, 0, it.g, krow, sy.k_full + 8 * s);
+                        tma_load_3d(dst + kKPanel, &tmK, 64, it.g, krow, sy.k_full + 8 * s);
+                    }
+                }
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            uint32_t kc = 0, sc = 0, qn = 0;
+            for (int64_t w = blockIdx.x; w < n_items; w += gridDim.x) {
+                const Item it = decode<QT>(w, p, cu_tiles, n_tiles);
+                if (it.nkt == 0) continue;
+                bool ok = wait_bar(sy, sy.q_full, qn & 1, 3);
+                ++qn;
+                tc_fence_after();
+                for (int pass = 0; pass < 2; ++pass) {
+                    for (int32_t kt = 0; kt < it.nkt; ++kt, ++kc, ++sc) {
+                        const uint32_t s = kc % kStages;
+                        const uint32_t buf = sc & 1;
+                        ok = wait_bar(sy, sy.k_full + 8 * s, (kc / kStages) & 1, 4) && ok;
+                        ok = wait_bar(sy, sy.s_empty + 8 * buf, ((sc >> 1) & 1) ^ 1, 5) && ok;
+                        tc_fence_after();
+                        if (!ok) continue;
+                        const uint32_t d = tmem + buf * 256;
+                        const uint32_t kb = sbase + kOffK + s * kKStage;
+                        if (pass == 0) {
+#pragma unroll
+                            for (int kk = 0; kk < kD / 16; ++kk) {
+                                const uint32_t koff = (kk >> 2) * kKPanel + (kk & 3) * 32;
+                                const uint32_t qoff = (kk >> 2) * kQPanel + (kk & 3) * 32;
+                                const uint64_t bdesc = desc_kmajor_sw128(kb + koff);
+                                umma_bf16(d, desc_kmajor_sw128(sbase + qoff), bdesc, kIdescP1, kk > 0);
+                                umma_bf16(d + 128, desc_kmajor_sw128(sbase + qoff + 128 * 128), bdesc,
+                                          kIdescP1, kk > 0);
+                            }
+                        } else {
+#pragma unroll
+                            for (int kk = 0; kk < kD / 16; ++kk) {
+                                const uint32_t koff = (kk >> 2) * kKPanel + (kk & 3) * 32;
+                                const uint32_t qoff = (kk >> 2) * kQPanel + (kk & 3) * 32;
+                                umma_bf16(d, desc_kmajor_sw128(kb + koff), desc_kmajor_sw128(sbase + qoff),
+                                          kIdescP2, kk > 0);
+                            }
+                        }
+                        umma_commit(sy.k_empty + 8 * s);
+                        umma_commit(sy.s_full + 8 * buf);
+                    }
+                }
+                if (ok) umma_commit(sy.q_empty);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int tid = threadIdx.x;        // 0..255
+        const int wg = warp >> 2;           // which half of the tile
+        const int wq = warp & 3;            // TMEM lane quarter
+        const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
+        const float c = p.c;
+        uint32_t sc = 0;
+        for (int64_t w = blockIdx.x; w < n_items; w += gridDim.x) {
+            const Item it = decode<QT>(w, p, cu_tiles, n_tiles);
+            named_bar_sync(kEpiBarrier, kEpiWarps * 32);  // previous tile done with lim_s/stats
+            if (tid < QT)
+                lim_s[tid] = tid < it.nq ? visible(it.local0 + tid, it.q_len, it.k_len, p.causal) : 0;
+            named_bar_sync(kEpiBarrier, kEpiWarps * 32);
+            __nv_bfloat16 *out_g = p.out + (int64_t)it.g * p.T * p.out_stride;
+
+            if (it.nkt > 0) {
+                // ---------------- pass 1: softmax statistics of row r = (token, head)
+                const int r = wg * 128 + wq * 32 + lane;
+                const int32_t lim_r = lim_s[r / G];
+                float m = -INFINITY, l = 0.f;
+                for (int32_t kt = 0; kt < it.nkt; ++kt, ++sc) {
+                    const uint32_t buf = sc & 1;
+                    wait_bar(sy, sy.s_full + 8 * buf, (sc >> 1) & 1, 6);
+                    tc_fence_after();
+                    const uint32_t ta = tmem + lane_base + buf * 256 + wg * 128;
+#pragma unroll 1
+                    for (int half = 0; half < 2; ++half) {
+                        float v[64];
+                        tmem_ld32(ta + half * 64, *reinterpret_cast<float(*)[32]>(&v[0]));
+                        tmem_ld32(ta + half * 64 + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+                        tmem_wait_ld();
+                        const int32_t col0 = kt * kBN + half * 64;
+                        if (col0 + 64 > lim_r) {
+#pragma unroll
+                            for (int i = 0; i < 64; ++i)
+                                if (col0 + i >= lim_r) v[i] = -INFINITY;
+                        }
+                        float mx = v[0];
+#pragma unroll
+                        for (int i = 1; i < 64; ++i) mx = fmaxf(mx, v[i]);
+                        const float m_new = fmaxf(m, mx);
+                        if (m_new != -INFINITY) {
+                            const float mc = m_new * c;
+                            float sum = 0.f;
+#pragma unroll
+                            for (int i = 0; i < 64; ++i) sum += ex2(fmaf(v[i], c, -mc));
+                            l = (m == -INFINITY ? 0.f : l * ex2((m - m_new) * c)) + sum;
+                            m = m_new;
+                        }
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(sy.s_empty + 8 * buf);
+                }
+                stats[r] = (l > 0.f) ? fmaf(m, c, log2f(l)) : INFINITY;
+                named_bar_sync(kEpiBarrier, kEpiWarps * 32);
+
+                // ---------------- pass 2: key j = this thread's TMEM lane
+                for (int32_t kt = 0; kt < it.nkt; ++kt, ++sc) {
+                    const uint32_t buf = sc & 1;
+                    wait_bar(sy, sy.s_full + 8 * buf, (sc >> 1) & 1, 7);
+                    tc_fence_after();
+                    const uint32_t ta = tmem + lane_base + buf * 256 + wg * 128;
+                    const int32_t j = kt * kBN + wq * 32 + lane;
+                    const bool j_in_row = j < p.out_stride;
+#pragma unroll 1
+                    for (int ch = 0; ch < 4; ++ch) {
+                        float v[32];
+                        tmem_ld32(ta + ch * 32, v);
+                        tmem_wait_ld();
+                        const int col0 = wg * 128 + ch * 32;  // tile row index of v[0]
+#pragma unroll
+                        for (int qi = 0; qi < 32 / G; ++qi) {
+                            const int tq = (col0 >> __builtin_ctz(G)) + qi;
+                            float acc = 0.f;
+#pragma unroll
+                            for (int h = 0; h < G; ++h)
+                                acc += ex2(fmaf(v[qi * G + h], c, -stats[col0 + qi * G + h]));
+                            if (tq < it.nq && j_in_row) {
+                                const float o = j < lim_s[tq] ? fmaxf(acc, 0.f) : 0.f;
+                                out_g[(it.t0 + tq) * p.out_stride + j] = __float2bfloat16_rn(o);
+                            }
+                        }
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(sy.s_empty + 8 * buf);
+                }
+            }
+            // ---------------- zero the columns past the computed key tiles
+            {
+                const int64_t c0 = (int64_t)it.nkt * kBN;
+                const int64_t ncol = p.out_stride - c0;
+                if (ncol > 0) {
+                    const int64_t per_row = ncol / 8;  // 16-byte chunks (out_stride % 128 == 0)
+                    const int64_t total = per_row * it.nq;
+                    const uint4 z = make_uint4(0, 0, 0, 0);
+                    for (int64_t e = tid; e < total; e += kEpiWarps * 32) {
+                        const int64_t tq = e / per_row, cc = e - tq * per_row;
+                        uint4 *dst = reinterpret_cast<uint4 *>(out_g + (it.t0 + tq) * p.out_stride + c0) + cc;
+                        *dst = z;
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        if (*abort_flag) {
+            // give TMA/UMMA work already in flight time to land before TMEM is released
+            const uint64_t t0 = globaltimer_ns();
+            while (globaltimer_ns() - t0 < 2000000ull) {
+            }
+        }
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// Prologue: per-sequence tile prefix into the workspace, status := 0, and
+// zero rows of `out` that no sequence covers (tokens outside
+// [cu_q[0], cu_q[n_seq]) keep the reference's torch.zeros value).
+__global__ void __launch_bounds__(1024)
+stage1_prologue(const int32_t *__restrict__ cu_q, int32_t n_seq, int32_t QT, int32_t *ws,
+                __nv_bfloat16 *out, int64_t T, int32_t Hk, int64_t out_stride) {
+    __shared__ int32_t warp_sums[32];
+    __shared__ int32_t carry_s;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) {
+        ws[0] = 0;
+        carry_s = 0;
+    }
+    __syncthreads();
+    int32_t *cu_tiles = ws + kWsTiles;
+    for (int32_t base = 0; base < n_seq; base += 1024) {
+        const int32_t b = base + tid;
+        int32_t cnt = 0;
+        if (b < n_seq) {
+            const int32_t len = cu_q[b + 1] - cu_q[b];
+            cnt = len > 0 ? (len + QT - 1) / QT : 0;
+        }
+        int32_t x = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) warp_sums[warp] = x;
+        __syncthreads();
+        if (warp == 0) {
+            int32_t s = warp_sums[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int32_t y = __shfl_up_sync(0xffffffffu, s, o);
+                if (lane >= o) s += y;
+            }
+            warp_sums[lane] = s;  // inclusive over warps
+        }
+        __syncthreads();
+        const int32_t carry = carry_s;
+        const int32_t excl = carry + (warp > 0 ? warp_sums[warp - 1] : 0) + x - cnt;
+        if (b < n_seq) cu_tiles[b] = excl;
+        __syncthreads();
+        if (tid == 0) carry_s = carry + warp_sums[31];
+        __syncthreads();
+    }
+    if (tid == 0) cu_tiles[n_seq] = carry_s;
+    // rows outside every sequence
+    const int64_t lo = n_seq > 0 ? cu_q[0] : T, hi = n_seq > 0 ? cu_q[n_seq] : T;
+    const int64_t per_row = out_stride / 8;
+    for (int32_t g = 0; g < Hk; ++g) {
+        for (int64_t t = 0; t < T; ++t) {
+            if (t >= lo && t < hi) {
+                t = hi - 1;
+                continue;
+            }
+            uint4 *row = reinterpret_cast<uint4 *>(out + ((int64_t)g * T + t) * out_stride);
+            for (int64_t e = tid; e < per_row; e += 1024) row[e] = make_uint4(0, 0, 0, 0);
+        }
+    }
+}
+
+// ------------------------------------------------------------------ host side
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+    return fn;
+}
+
+// 3-D bf16 map over [dim2][dim1][dim0] with a box of (64, box1, box2), 128-byte swizzle.
+int make_map(CUtensorMap *m, const void *base, uint64_t dim0, uint64_t dim1, uint64_t dim2,
+             uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box1, uint32_t box2) {
+    auto enc = get_encode_fn();
+    if (!enc) {
+        unum::set_error("cuTensorMapEncodeTiled unavailable from the driver");
+        return UNUM_ERR_CUDA;
+    }
+    cuuint64_t gdim[3] = {dim0, dim1, dim2};
+    cuuint64_t gstride[2] = {stride1_bytes, stride2_bytes};
+    cuuint32_t box[3] = {64, box1, box2};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), gdim, gstride,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        unum::set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
+        return UNUM_ERR_CUDA;
+    }
+    return UNUM_OK;
+}
+
+template <int G>
+int launch_main(const CUtensorMap &mq, const CUtensorMap &mk, const Params &p, int64_t T,
+                cudaStream_t s) {
+    auto kern = stage1_kernel<G>;
+    UNUM_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+    constexpr int QT = kRows / G;
+    const int64_t items_ub = ((T + QT - 1) / QT + p.n_seq) * p.Hk;
+    const int64_t sms = unum::sm_count();
+    const int grid = (int)(items_ub < sms ? items_ub : sms);
+    kern<<<grid, kThreads, kSmemBytes, s>>>(mq, mk, p);
+    return unum::check_launch("stage1_kernel");
+}
+
+}  // namespace
+
+extern "C" size_t unum_stage1_workspace_size(int64_t n_seq) {
+    if (n_seq < 0) n_seq = 0;
+    return (size_t)(((kWsTiles + n_seq + 1) * 4 + 15) / 16 * 16);
+}
+
+extern "C" int unum_infllmv2_attn_stage1(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st,
+                                         int64_t q_sh, const void *k, int64_t Tk, int64_t Hk,
+                                         int64_t k_st, int64_t k_sh, const int32_t *cu_seqlens_q,
+                                         const int32_t *cu_seqlens_k, int64_t n_seq,
+                                         float softmax_scale, int causal, void *out,
+                                         int64_t out_stride, void *workspace,
+                                         size_t workspace_bytes, void *stream) {
+    unum::clear_error();
+    UNUM_CHECK_ARG(T >= 0 && Tk >= 0 && Hq > 0 && Hk > 0 && n_seq >= 0 && out_stride >= 0,
+                   "bad sizes");
+    UNUM_CHECK_ARG(Hq % Hk == 0, "n_heads (%lld) must be a multiple of n_kv_heads (%lld)",
+                   (long long)Hq, (long long)Hk);
+    if (T == 0 || out_stride == 0) return UNUM_OK;
+    if (D != kD) {
+        unum::set_error("head_dim %lld not supported (only 128)", (long long)D);
+        return UNUM_ERR_UNSUPPORTED;
+    }
+    const int64_t G = Hq / Hk;
+    if (!(G == 1 || G == 2 || G == 4 || G == 8 || G == 16 || G == 32)) {
+        unum::set_error("head group size %lld not supported (1,2,4,8,16,32)", (long long)G);
+        return UNUM_ERR_UNSUPPORTED;
+    }
+    UNUM_CHECK_ARG(out_stride % 128 == 0, "out_stride must be a multiple of 128");
+    UNUM_CHECK_ARG(q && out && cu_seqlens_q && cu_seqlens_k, "null pointer argument");
+    UNUM_CHECK_ARG(unum::aligned16(out), "out must be 16-byte aligned");
+    UNUM_CHECK_ARG(T < (int64_t)1 << 31 && Tk < (int64_t)1 << 31, "too many tokens");
+    if (!workspace || workspace_bytes < unum_stage1_workspace_size(n_seq)) {
+        unum::set_error("workspace of %zu bytes needed", unum_stage1_workspace_size(n_seq));
+        return UNUM_ERR_WORKSPACE;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    int32_t *ws = (int32_t *)workspace;
+    const int QT = (int)(kRows / G);
+    stage1_prologue<<<1, 1024, 0, s>>>(cu_seqlens_q, (int32_t)n_seq, QT, ws,
+                                       (__nv_bfloat16 *)out, T, (int32_t)Hk, out_stride);
+    if (int rc = unum::check_launch("stage1_prologue")) return rc;
+    if (n_seq == 0) return UNUM_OK;
+    if (Tk == 0) {  // no compressed keys anywhere: every row is zero
+        UNUM_CHECK_CUDA(cudaMemsetAsync(out, 0, (size_t)Hk * T * out_stride * 2, s));
+        return UNUM_OK;
+    }
+    UNUM_CHECK_ARG(k != nullptr, "null k");
+    UNUM_CHECK_ARG(unum::aligned16(q) && unum::aligned16(k), "q and k must be 16-byte aligned");
+    UNUM_CHECK_ARG(q_st % 8 == 0 && q_sh % 8 == 0 && k_st % 8 == 0 && k_sh % 8 == 0,
+                   "q/k strides must be multiples of 8 elements");
+    CUtensorMap mq, mk;
+    if (int rc = make_map(&mq, q, (uint64_t)D, (uint64_t)Hq, (uint64_t)T, (uint64_t)q_sh * 2,
+                          (uint64_t)q_st * 2, (uint32_t)G, (uint32_t)QT))
+        return rc;
+    if (int rc = make_map(&mk, k, (uint64_t)D, (uint64_t)Hk, (uint64_t)Tk, (uint64_t)k_sh * 2,
+                          (uint64_t)k_st * 2, 1, kBN))
+        return rc;
+    Params p;
+    p.cu_q = cu_seqlens_q;
+    p.cu_k = cu_seqlens_k;
+    p.ws = ws;
+    p.out = (__nv_bfloat16 *)out;
+    p.T = T;
+    p.out_stride = out_stride;
+    p.n_seq = (int32_t)n_seq;
+    p.Hk = (int32_t)Hk;
+    p.causal = causal ? 1 : 0;
+    p.c = softmax_scale * kLog2e;
+    switch (G) {
+        case 1: return launch_main<1>(mq, mk, p, T, s);
+        case 2: return launch_main<2>(mq, mk, p, T, s);
+        case 4: return launch_main<4>(mq, mk, p, T, s);
+        case 8: return launch_main<8>(mq, mk, p, T, s);
+        case 16: return launch_main<16>(mq, mk, p, T, s);
+        default: return launch_main<32>(mq, mk, p, T, s);
+    }
+}
+
+extern "C" int unum_stage1_status(const void *workspace, void *stream, int32_t *status_out) {
+    unum::clear_error();
+    UNUM_CHECK_ARG(workspace && status_out, "null pointer argument");
+    cudaStream_t s = (cudaStream_t)stream;
+    UNUM_CHECK_CUDA(cudaMemcpyAsync(status_out, workspace, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    UNUM_CHECK_CUDA(cudaStreamSynchronize(s));
+    return UNUM_OK;
+}
