@@ -33,7 +33,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-L_SEQ = 131072
+L_SEQ = 131072  # tokens of the prefill sequence (--seqlen overrides, for small profiling cases)
 HQ, HK, D = 32, 2, 128
 NKC = (L_SEQ - 32) // 16 + 1  # 8191 compressed keys
 TOPK = 64
@@ -41,7 +41,9 @@ INIT_BLOCKS, LOCAL_BLOCKS = 1, 2
 METRIC = "block-selection tokens/s at 128k prefill (stage1+pool+topk+get_block_table)"
 
 
-def visible_counts(L=L_SEQ, k_len=NKC):
+def visible_counts(L=None, k_len=None):
+    L = L_SEQ if L is None else L
+    k_len = NKC if k_len is None else k_len
     lq = np.arange(L, dtype=np.int64)
     off = np.trunc((lq - 15) / 16).astype(np.int64) + k_len - (L - 15) // 16
     return np.clip(off, 0, k_len)
@@ -63,6 +65,12 @@ def algorithmic_bytes():
         "get_block_table": T * HK * TOPK * 64 * 4 + HK * T * TOPK * 4 + 8 * T + 4 * L_SEQ,
         "stage1_out": HK * T * W * 2,
     }
+
+
+def workload_name():
+    tag = "C3: 128k-token" if L_SEQ == 131072 else f"{L_SEQ}-token (reduced C3)"
+    return (f"{tag} causal prefill, 32 q-heads / 2 kv-heads, d=128, k_cmp {NKC}, "
+            f"NB {(L_SEQ + 63) // 64}, top-64, per-token block table [1,{L_SEQ}]")
 
 
 def load_peaks():
@@ -101,7 +109,7 @@ class ClockSampler:
                  "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.fh,
+                 "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.fh,
                 stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -304,8 +312,7 @@ def run_ours(args):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) q/k_cmp, random-permutation block table)",
-            "config": {"workload": "C3: 128k-token causal prefill, 32 q-heads / 2 kv-heads, d=128, "
-                                   "k_cmp 8191, NB 2048, top-64, per-token block table [1,131072]",
+            "config": {"workload": workload_name(),
                        "tokens_per_gpu": L_SEQ, "parallelism": f"dp{world} (one sequence per GPU)",
                        "l2": "inputs larger than L2 (q 1.07 GB, scores 4.3 GB, slots 4.3 GB)"},
             "roofline": {"bound": "tensor", "kernel": "stage1", "achieved": s1_tf,
@@ -399,8 +406,7 @@ def run_reference(args):
         "warmup": args.warmup, "ms_per_step": L_SEQ / v * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "reference",
         "data": "synthetic (seeded N(0,1) q/k_cmp, random-permutation block table)",
-        "config": {"workload": "C3: 128k-token causal prefill, 32 q-heads / 2 kv-heads, d=128, "
-                               "k_cmp 8191, NB 2048, top-64, per-token block table [1,131072]",
+        "config": {"workload": workload_name(),
                    "host": "CPU reference path (C port of the reference semantics, oracle/)"},
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": steps[0]["cores"],
                          "kind": "port", "sample": steps[0]["sample"]},
@@ -412,13 +418,20 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-sample", type=int, default=8192,
                     help="tokens of the CPU-baseline sample (0: skip)")
     ap.add_argument("--ref-sample", type=int, default=2048)
+    ap.add_argument("--seqlen", type=int, default=131072,
+                    help="prefill length (default: the 128k headline workload)")
     args = ap.parse_args()
+    global L_SEQ, NKC
+    L_SEQ = args.seqlen
+    NKC = (L_SEQ - 32) // 16 + 1
+    args.cpu_sample = min(args.cpu_sample, L_SEQ)
+    args.ref_sample = min(args.ref_sample, L_SEQ)
     if args.impl == "reference":
         run_reference(args)
     else:
