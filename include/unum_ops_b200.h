@@ -129,7 +129,8 @@ int unum_topk_blocks(const void *scores, int dtype, int64_t rows, int64_t NB,
  *   key j is visible iff j < clamp((lq-15)/16 + k_len - (q_len-15)/16, 0, k_len)
  *   (C integer division, lq = t - cu_q[b]).
  *
- * Requirements: D == 128; G a power of two <= 256; q, k 16-byte aligned with
+ * Requirements: D == 128; G in {2, 4, 8, 16, 32} (the reference's Triton
+ * kernel itself needs G >= 16 for its tl.dot); q, k 16-byte aligned with
  * 16-byte-multiple strides.  workspace: device memory of at least
  * unum_stage1_workspace_size(n_seq) bytes, 16-byte aligned; its contents on
  * entry do not matter.  Calls sharing a workspace must be stream-ordered.

@@ -7,61 +7,80 @@
 // or 0 when pos is negative, past seqlen_q[bs] or past token_pos_in_bs[t].
 //
 // B200 design: the path is a pure HBM write stream (T*H*K*256 bytes out, the
-// table row of a sequence stays in L2).  One CTA walks one token at a time
-// (grid-stride over tokens); each thread produces 4 consecutive slot ids and
-// writes them with one 16-byte streaming store, so a warp writes 512
-// contiguous bytes.  Table reads are 16-byte vector loads whenever the four
-// positions are valid and inside the row.
+// table row of a sequence stays in L2).  One warp owns one (token, head) output
+// row of K*64 ids; a half-warp covers one selected block, each lane producing 4
+// consecutive ids with one 16-byte streaming store, so a warp writes 512
+// contiguous bytes per step.  Index arithmetic is 32-bit and division-free
+// inside a row; four steps are unrolled so their table loads are in flight
+// together.  Table reads are 16-byte vector loads whenever the four positions
+// are valid and inside the row.
 #include "common.cuh"
 
 namespace {
 
 constexpr int kBlock = 64;   // kSparseBlockSize (get_table_torch.py:13)
-constexpr int kThreads = 256;
+constexpr int kWarps = 8;
+constexpr int kUnroll = 4;
 
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kWarps * 32)
 get_block_table_kernel(const int32_t *__restrict__ topk, int64_t H, int64_t T, int64_t K,
                        int64_t ts_h, int64_t ts_t, int64_t ts_k,
                        const int32_t *__restrict__ table, int64_t B, int64_t L, int64_t bt_stride,
                        const int32_t *__restrict__ token_to_bs, const int32_t *__restrict__ pos_in_bs,
                        int pos_scalar, const int32_t *__restrict__ seqlen, int seqlen_scalar,
                        uint32_t head_group, bool vec_ok, int32_t *__restrict__ out) {
-    const int64_t items = H * K * (kBlock / 4);  // int4 items per token
-    for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
+    const int lane = threadIdx.x & 31;
+    const int64_t rows = T * H;
+    const int32_t items = (int32_t)(K * (kBlock / 4));  // int4 items per row
+    const int32_t q4 = (lane & 15) * 4;                  // first of this lane's 4 positions in a block
+    const int32_t Lm1 = (int32_t)(L - 1);
+    for (int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); row < rows;
+         row += (int64_t)gridDim.x * kWarps) {
+        const int64_t t = row / H;
+        const uint32_t h = (uint32_t)(row - t * H);
         const int32_t bs = __ldg(token_to_bs + t);
         const bool bs_ok = bs >= 0 && bs < B;
         const int32_t lim_pos = pos_scalar ? __ldg(pos_in_bs) : __ldg(pos_in_bs + t);
         const int32_t sl = seqlen_scalar ? __ldg(seqlen) : (bs_ok ? __ldg(seqlen + bs) : 0);
         const int32_t lim = bs_ok ? min(lim_pos, sl) : INT32_MIN;  // valid iff 0 <= pos < lim
         const int32_t *trow = table + (bs_ok ? (int64_t)bs * bt_stride : 0);
-        int4 *orow = reinterpret_cast<int4 *>(out + t * H * K * kBlock);
-        for (int64_t e = threadIdx.x; e < items; e += kThreads) {
-            const int64_t slot = e >> 4;          // h*K + k
-            const int q4 = (int)(e & 15) * 4;     // first of 4 positions inside the block
-            const int64_t h = slot / K;
-            const int64_t k = slot - h * K;
-            const int32_t idx = __ldg(topk + h * ts_h + t * ts_t + k * ts_k);
-            const int32_t p0 = (int32_t)((uint32_t)idx * (uint32_t)kBlock + (uint32_t)q4);
-            const uint32_t hh = (uint32_t)h;
-            int4 v;
-            if (p0 >= 0 && p0 <= INT32_MAX - 3 && p0 + 3 < lim && p0 + 3 < L && vec_ok) {
-                const int4 tv = __ldg(reinterpret_cast<const int4 *>(trow + p0));
-                v.x = (int32_t)(head_group * (uint32_t)tv.x + hh);
-                v.y = (int32_t)(head_group * (uint32_t)tv.y + hh);
-                v.z = (int32_t)(head_group * (uint32_t)tv.z + hh);
-                v.w = (int32_t)(head_group * (uint32_t)tv.w + hh);
-            } else {
-                int32_t r[4];
+        const int32_t *tk = topk + (int64_t)h * ts_h + t * ts_t;
+        int4 *orow = reinterpret_cast<int4 *>(out) + row * items;
+        for (int32_t e0 = 0; e0 < items; e0 += 32 * kUnroll) {
+            int32_t p0[kUnroll];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int32_t p = (int32_t)((uint32_t)p0 + (uint32_t)i);
-                    const bool valid = p >= 0 && p < lim;
-                    const int64_t sp = p < 0 ? 0 : (p > L - 1 ? L - 1 : p);  // clamp (get_table_torch.py:35)
-                    r[i] = valid ? (int32_t)(head_group * (uint32_t)__ldg(trow + sp) + hh) : 0;
-                }
-                v = make_int4(r[0], r[1], r[2], r[3]);
+            for (int u = 0; u < kUnroll; ++u) {
+                const int32_t e = e0 + u * 32 + lane;
+                const int32_t idx = e < items ? __ldg(tk + (int64_t)(e >> 4) * ts_k) : -1;
+                p0[u] = (int32_t)((uint32_t)idx * (uint32_t)kBlock + (uint32_t)q4);
             }
-            __stcs(orow + e, v);
+            int4 v[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int32_t p = p0[u];
+                if (vec_ok && p >= 0 && p <= INT32_MAX - 3 && p + 3 < lim && p + 3 <= Lm1) {
+                    const int4 tv = __ldg(reinterpret_cast<const int4 *>(trow + p));
+                    v[u].x = (int32_t)(head_group * (uint32_t)tv.x + h);
+                    v[u].y = (int32_t)(head_group * (uint32_t)tv.y + h);
+                    v[u].z = (int32_t)(head_group * (uint32_t)tv.z + h);
+                    v[u].w = (int32_t)(head_group * (uint32_t)tv.w + h);
+                } else {
+                    int32_t r[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int32_t pi = (int32_t)((uint32_t)p + (uint32_t)i);
+                        const bool valid = pi >= 0 && pi < lim;
+                        const int32_t sp = pi < 0 ? 0 : (pi > Lm1 ? Lm1 : pi);  // clamp (get_table_torch.py:35)
+                        r[i] = valid ? (int32_t)(head_group * (uint32_t)__ldg(trow + sp) + h) : 0;
+                    }
+                    v[u] = make_int4(r[0], r[1], r[2], r[3]);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int32_t e = e0 + u * 32 + lane;
+                if (e < items) __stcs(orow + e, v[u]);
+            }
         }
     }
 }
@@ -82,11 +101,14 @@ extern "C" int unum_get_block_table(const int32_t *topk_idx, int64_t H, int64_t 
                    "null pointer argument");
     UNUM_CHECK_ARG(B > 0 && L > 0 && block_table, "block_table must be non-empty");
     UNUM_CHECK_ARG(unum::aligned16(out), "out must be 16-byte aligned");
-    UNUM_CHECK_ARG(H * K * kBlock <= (int64_t)INT32_MAX, "H*K*64 too large");
+    UNUM_CHECK_ARG(K * kBlock <= (int64_t)INT32_MAX / 4, "K too large");
+    UNUM_CHECK_ARG(L <= (int64_t)INT32_MAX, "block_table row too long");
     const bool vec_ok = unum::aligned16(block_table) && (bt_stride % 4 == 0);
-    const int64_t max_grid = (int64_t)unum::sm_count() * 16;
-    const int grid = (int)(T < max_grid ? T : max_grid);
-    get_block_table_kernel<<<grid, kThreads, 0, (cudaStream_t)stream>>>(
+    const int64_t rows = T * H;
+    const int64_t want = (rows + kWarps - 1) / kWarps;
+    const int64_t cap = (int64_t)unum::sm_count() * 32;
+    const int grid = (int)(want < cap ? want : cap);
+    get_block_table_kernel<<<grid, kWarps * 32, 0, (cudaStream_t)stream>>>(
         topk_idx, H, T, K, ts_h, ts_t, ts_k, block_table, B, L, bt_stride, token_to_bs,
         token_pos_in_bs, pos_is_scalar, seqlen_q, seqlen_is_scalar, (uint32_t)head_group, vec_ok,
         out);

@@ -9,10 +9,11 @@
 //
 // B200 design: an HBM stream (the whole score row is read once, the pooled
 // row written once).  One warp owns one (head, token) row.  On the common
-// layout (sp == 4, 16-byte aligned rows) each lane loads one 16-byte vector of
-// scores per step and produces 16/sizeof(T)/4 pooled values; the window's
-// left element (c = 4j-1) is the previous lane's last element, fetched with a
-// shuffle, so every score is read from HBM exactly once.  Every other layout
+// layout (sp == 4, 16-byte aligned rows) each lane loads 16-byte vectors of
+// scores (two in flight per step) and produces 16/sizeof(T)/4 pooled values
+// per vector; the window's left element (c = 4j-1) is the previous lane's
+// last element, fetched with a shuffle, so every score is read from HBM
+// exactly once.  Only a row's last vector needs per-element masking.  Every other layout
 // (odd flat strides as in the reference's own tests, other pooling ratios)
 // takes a scalar path with the same results.
 #include <cuda_bf16.h>
@@ -46,6 +47,24 @@ __device__ __forceinline__ int find_seq(const int32_t *__restrict__ cu_q, int64_
     return (int)lo;
 }
 
+template <typename T> struct Pack2;  // two outputs stored as one word
+template <> struct Pack2<float> { using type = float2; };
+template <> struct Pack2<__nv_bfloat16> { using type = __nv_bfloat162; };
+template <> struct Pack2<__half> { using type = __half2; };
+
+template <typename T>
+__device__ __forceinline__ void store2(T *p, float a, float b, bool paired) {
+    if (paired) {
+        typename Pack2<T>::type v;
+        v.x = from_f<T>(a);
+        v.y = from_f<T>(b);
+        *reinterpret_cast<typename Pack2<T>::type *>(p) = v;
+    } else {
+        p[0] = from_f<T>(a);
+        p[1] = from_f<T>(b);
+    }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kWarps * 32)
 max_pool_kernel(const T *__restrict__ in, int64_t numel, int64_t H, int64_t T_, int64_t fs,
@@ -57,86 +76,110 @@ max_pool_kernel(const T *__restrict__ in, int64_t numel, int64_t H, int64_t T_, 
     constexpr int OPV = VEC / 4;         // pooled outputs per load when sp == 4
     const int lane = threadIdx.x & 31;
     const int64_t rows = H * T_;
-    const int64_t wid = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
-    const int64_t nw = (int64_t)gridDim.x * kWarps;
     const int64_t ksize = sp + 1;
-    for (int64_t row = wid; row < rows; row += nw) {
+    const int32_t nb = (int32_t)NB;
+    const bool pair_ok = (NB % 2) == 0;  // 2 outputs per lane per vector: aligned word stores
+    for (int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); row < rows;
+         row += (int64_t)gridDim.x * kWarps) {
         const int64_t h = row / T_, t = row - h * T_;
         const int b = find_seq(cu_q, n_seq, t);
-        int64_t k_len = 0, off_bq = 0;
+        int32_t k_len = 0, off_bq = 0;
         if (b >= 0) {
-            k_len = (int64_t)(__ldg(cu_k + b + 1) - __ldg(cu_k + b)) + __ldg(cache_lens + b);
-            off_bq = (t - __ldg(cu_q + b)) / block_size;
+            k_len = (__ldg(cu_k + b + 1) - __ldg(cu_k + b)) + __ldg(cache_lens + b);
+            off_bq = (int32_t)((t - __ldg(cu_q + b)) / block_size);
         }
         const int64_t base = h * T_ * fs + t * fs;
+        const T *src = in + base;
+        // readable scores of this row: positions [0, avail)
+        const int64_t room = numel - base;
+        const int32_t avail = (int32_t)(room < (int64_t)k_len ? (room > 0 ? room : 0) : k_len);
         T *orow = out + row * NB;
-        // Blocks at or past j_end have an empty window (4j-1 >= k_len).
-        int64_t j_end = k_len > 0 ? (k_len + 1 + sp - 1) / sp : 0;  // first j with j*sp-1 >= k_len
-        if (j_end > NB) j_end = NB;
-        auto finish = [&](int64_t j, float mx, bool has) {
-            const bool minf = (j < init_blocks) || (off_bq >= j && off_bq <= j + local_blocks);
-            orow[j] = from_f<T>(minf ? INFINITY : (has ? mx : -INFINITY));
-        };
-        int64_t j_done = 0;
-        if (vec_ok && sp == 4) {
-            // vector path over outputs [0, j_end): chunk c covers scores [c*VEC, c*VEC+VEC)
-            const int64_t n_chunks = (j_end + OPV - 1) / OPV;
-            float carry = -INFINITY;  // score c*VEC-1 of the first lane of the next step
-            for (int64_t c0 = 0; c0 < n_chunks; c0 += 32) {
-                const int64_t c = c0 + lane;
-                float e[VEC];
-                const int64_t p0 = c * VEC;  // first score position of this chunk
-                if (c < n_chunks && base + p0 + VEC <= numel) {
-                    const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(in + base + p0));
-                    const T *tv = reinterpret_cast<const T *>(&raw);
+        const int32_t init_b = (int32_t)init_blocks, local_b = (int32_t)local_blocks;
+        // Blocks at or past j_end have an empty window (j*sp-1 >= k_len).
+        int32_t j_end = k_len > 0 ? (int32_t)((k_len + sp) / sp) : 0;
+        if (j_end > nb) j_end = nb;
+        auto masked = [&](int32_t j) { return j < init_b || (off_bq >= j && off_bq <= j + local_b); };
+        int32_t j_done = 0;
+        if (vec_ok && sp == 4 && OPV == 2) {
+            // 16-bit scores: a 16-byte vector = 8 scores = the windows of 2 blocks
+            const int32_t n_chunks = (j_end + 1) / 2;
+            float carry = -INFINITY;  // score 8c-1 for lane 0 of the next step
+            for (int32_t c0 = 0; c0 < n_chunks; c0 += 64) {
+                float e[2][8];
 #pragma unroll
-                    for (int i = 0; i < VEC; ++i) e[i] = to_f<T>(tv[i]);
-                } else {
+                for (int u = 0; u < 2; ++u) {
+                    const int32_t c = c0 + u * 32 + lane;
+                    const int32_t p0 = c * 8;
+                    if (c < n_chunks && p0 + 8 <= avail) {
+                        const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(src + p0));
+                        const T *tv = reinterpret_cast<const T *>(&raw);
 #pragma unroll
-                    for (int i = 0; i < VEC; ++i) {
-                        const int64_t off = base + p0 + i;
-                        e[i] = (c < n_chunks && off < numel) ? to_f<T>(in[off]) : -INFINITY;
+                        for (int i = 0; i < 8; ++i) e[u][i] = to_f<T>(tv[i]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+                            e[u][i] = (c < n_chunks && p0 + i < avail) ? to_f<T>(src[p0 + i]) : -INFINITY;
                     }
                 }
-                // mask positions at or past k_len (and the buffer end, handled above)
 #pragma unroll
-                for (int i = 0; i < VEC; ++i)
-                    if (p0 + i >= k_len) e[i] = -INFINITY;
-                float prev = __shfl_up_sync(0xffffffffu, e[VEC - 1], 1);
-                if (lane == 0) prev = carry;
-                carry = __shfl_sync(0xffffffffu, e[VEC - 1], 31);
-                if (c < n_chunks) {
-#pragma unroll
-                    for (int o = 0; o < OPV; ++o) {
-                        const int64_t j = c * OPV + o;
-                        if (j < j_end) {
-                            // window positions 4j-1 .. 4j+3 -> e[4o-1 .. 4o+3]
-                            float mx = (o == 0) ? (j == 0 ? -INFINITY : prev) : e[4 * o - 1];
-                            mx = fmaxf(mx, e[4 * o + 0]);
-                            mx = fmaxf(mx, e[4 * o + 1]);
-                            mx = fmaxf(mx, e[4 * o + 2]);
-                            mx = fmaxf(mx, e[4 * o + 3]);
-                            finish(j, mx, true);  // j < j_end: the window is non-empty
+                for (int u = 0; u < 2; ++u) {
+                    const int32_t c = c0 + u * 32 + lane;
+                    float prev = __shfl_up_sync(0xffffffffu, e[u][7], 1);
+                    if (lane == 0) prev = carry;
+                    carry = __shfl_sync(0xffffffffu, e[u][7], 31);
+                    if (c < n_chunks) {
+                        const int32_t j = 2 * c;  // outputs j and j+1
+                        float m0 = fmaxf(fmaxf(j == 0 ? -INFINITY : prev, e[u][0]),
+                                         fmaxf(fmaxf(e[u][1], e[u][2]), e[u][3]));
+                        float m1 = fmaxf(fmaxf(e[u][3], e[u][4]), fmaxf(fmaxf(e[u][5], e[u][6]), e[u][7]));
+                        m0 = masked(j) ? INFINITY : m0;          // j < j_end: window non-empty
+                        if (j + 1 < j_end) {
+                            m1 = masked(j + 1) ? INFINITY : m1;
+                            store2<T>(orow + j, m0, m1, pair_ok);
+                        } else {
+                            orow[j] = from_f<T>(m0);
                         }
                     }
                 }
             }
             j_done = j_end;
+        } else if (vec_ok && sp == 4) {
+            // fp32 scores: a 16-byte vector = 4 scores = the window of 1 block
+            float carry = -INFINITY;
+            for (int32_t c0 = 0; c0 < j_end; c0 += 32) {
+                const int32_t c = c0 + lane;
+                const int32_t p0 = c * 4;
+                float e[4];
+                if (c < j_end && p0 + 4 <= avail) {
+                    const float4 v = __ldg(reinterpret_cast<const float4 *>(src + p0));
+                    e[0] = v.x; e[1] = v.y; e[2] = v.z; e[3] = v.w;
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        e[i] = (c < j_end && p0 + i < avail) ? to_f<T>(src[p0 + i]) : -INFINITY;
+                }
+                float prev = __shfl_up_sync(0xffffffffu, e[3], 1);
+                if (lane == 0) prev = carry;
+                carry = __shfl_sync(0xffffffffu, e[3], 31);
+                if (c < j_end) {
+                    float m = fmaxf(fmaxf(c == 0 ? -INFINITY : prev, e[0]), fmaxf(fmaxf(e[1], e[2]), e[3]));
+                    orow[c] = from_f<T>(masked(c) ? INFINITY : m);
+                }
+            }
+            j_done = j_end;
         }
         // scalar path (general layouts) and the empty-window tail
-        for (int64_t j = j_done + lane; j < NB; j += 32) {
-            const int64_t ws = j * sp - 1;
+        for (int32_t j = j_done + lane; j < nb; j += 32) {
+            const int64_t ws = (int64_t)j * sp - 1;
             float mx = -INFINITY;
             for (int64_t ki = 0; ki < ksize; ++ki) {
                 const int64_t kp = ws + ki;
-                if (kp < 0 || kp >= k_len) continue;
-                const int64_t off = base + kp;
-                if (off < 0 || off >= numel) continue;
-                mx = fmaxf(mx, to_f<T>(in[off]));
+                if (kp < 0 || kp >= avail) continue;
+                mx = fmaxf(mx, to_f<T>(src[kp]));
             }
             const int64_t wlo = ws > 0 ? ws : 0;
             const int64_t whi = ws + ksize < k_len ? ws + ksize : k_len;
-            finish(j, mx, whi > wlo);
+            orow[j] = from_f<T>(masked(j) ? INFINITY : (whi > wlo ? mx : -INFINITY));
         }
     }
 }

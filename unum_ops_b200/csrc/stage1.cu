@@ -21,10 +21,14 @@
 //           leave the SM.  Results go straight to HBM as bf16.
 // The same Q/K shared-memory tiles serve both passes (operand roles swap).
 //
-// Warp roles (320 threads, one CTA per SM, persistent over tiles):
-//   warps 0-7  epilogue (TMEM -> registers -> softmax math -> global)
-//   warp 8     TMA producer (Q tile, 4-stage ring of K tiles)
-//   warp 9     TMEM allocator + single-thread UMMA issuer
+// Warp roles (576 threads, one CTA per SM, persistent over tiles):
+//   warps 0-15 epilogue (TMEM -> registers -> softmax math -> global), four
+//              per scheduler so TMEM-load and MUFU latencies overlap
+//   warp 16    TMA producer (Q tile, 4-stage ring of K tiles)
+//   warp 17    TMEM allocator + single-thread UMMA issuer
+// The epilogue issues packed f32x2 FMA/ADD (half the instructions of scalar
+// code) and computes a share of its exponentials with a polynomial on the FMA
+// pipe, the rest on the MUFU pipe.
 // TMEM holds two 256-column accumulator buffers so the tensor core fills one
 // while the epilogue drains the other.
 //
@@ -47,10 +51,10 @@ constexpr int kD = 128;            // head dim
 constexpr int kRows = 256;         // (token, head) rows per tile
 constexpr int kBN = 128;           // keys per key tile
 constexpr int kStages = 4;         // K ring depth
-constexpr int kEpiWarps = 8;
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr int kThreads = 320;
+constexpr int kEpiWarps = 16;      // 4 warpgroups, 64 accumulator columns each
+constexpr int kProducerWarp = 16;
+constexpr int kMmaWarp = 17;
+constexpr int kThreads = (kEpiWarps + 2) * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kEpiBarrier = 1;     // named barrier id for the 256 epilogue threads
 
@@ -60,7 +64,8 @@ constexpr uint32_t kKPanel = kBN * 128;            // 16 KB
 constexpr uint32_t kKStage = 2 * kKPanel;          // 32 KB
 constexpr uint32_t kOffK = kQBytes;
 constexpr uint32_t kOffStats = kOffK + kStages * kKStage;
-constexpr uint32_t kOffLim = kOffStats + kRows * 4;
+constexpr uint32_t kOffPart = kOffStats + kRows * 4;      // per-half (max, sum) of each row
+constexpr uint32_t kOffLim = kOffPart + 2 * kRows * 8;
 constexpr uint32_t kOffBar = kOffLim + kRows * 4;
 constexpr uint32_t kNumBars = 2 + 2 * kStages + 4;
 constexpr uint32_t kOffMisc = kOffBar + kNumBars * 8;
@@ -103,6 +108,48 @@ __device__ __forceinline__ int32_t visible(int32_t lq, int32_t q_len, int32_t k_
     if (!causal) return k_len;
     int32_t off = (lq - 15) / 16 + k_len - (q_len - 16 + 1) / 16;
     return off < 0 ? 0 : (off > k_len ? k_len : off);
+}
+
+// 2^x on the FMA pipe for two values at once, for a share of the
+// exponentials so the MUFU (ex2) pipe — 16 results per clock per SM — is not
+// the only unit doing them.  Split x = j + f with j = round(x) (adding
+// 1.5*2^23 rounds to an integer in the low mantissa bits) and f in
+// [-0.5, 0.5]; 2^f by a cubic fitted here to minimise the maximum relative
+// error on that interval (7.5e-5, far below the bf16 output precision); 2^j by
+// adding j to the exponent field.  Inputs are clamped to >= -126, so a masked
+// (-inf) score yields 2^-126 instead of 0 — negligible in any sum here; masked
+// outputs are written as exact zeros separately.
+__device__ __forceinline__ uint64_t exp2_fma2(uint64_t x2) {
+    float lo, hi;
+    f2_unpack(x2, lo, hi);
+    x2 = f2_pack(fmaxf(lo, -126.0f), fmaxf(hi, -126.0f));
+    const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);
+    const uint64_t nmagic = f2_pack(-12582912.0f, -12582912.0f);
+    const uint64_t t = f2_add(x2, magic);
+    const uint64_t f = f2_fma(f2_add(t, nmagic), f2_pack(-1.0f, -1.0f), x2);  // x - round(x)
+    uint64_t p = f2_fma(f2_pack(0.055171460f, 0.055171460f), f, f2_pack(0.24261086f, 0.24261086f));
+    p = f2_fma(p, f, f2_pack(0.69326097f, 0.69326097f));
+    p = f2_fma(p, f, f2_pack(0.99992812f, 0.99992812f));
+    const uint32_t plo = (uint32_t)p, phi = (uint32_t)(p >> 32);
+    const uint32_t tlo = (uint32_t)t, thi = (uint32_t)(t >> 32);
+    return (uint64_t)(plo + (tlo << 23)) | ((uint64_t)(phi + (thi << 23)) << 32);
+}
+
+__device__ __forceinline__ uint64_t exp2_mufu2(uint64_t x2) {
+    float lo, hi;
+    f2_unpack(x2, lo, hi);
+    return f2_pack(ex2(lo), ex2(hi));
+}
+
+// Pair p of a 64-value strip uses the polynomial when p % kPolyMod == kPolyMod-1.
+#ifndef UNUM_POLY_MOD
+#define UNUM_POLY_MOD 4
+#endif
+constexpr int kPolyMod = UNUM_POLY_MOD;
+template <int P>
+__device__ __forceinline__ uint64_t exp2_pair(uint64_t x2) {
+    return (kPolyMod > 0 && P % (kPolyMod > 0 ? kPolyMod : 1) == kPolyMod - 1) ? exp2_fma2(x2)
+                                                                               : exp2_mufu2(x2);
 }
 
 template <int QT>
@@ -156,7 +203,7 @@ __device__ __forceinline__ bool wait_bar(const Sync &s, uint32_t bar, uint32_t p
 }
 
 template <int G>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 1)  // 18 warps: at most 96 registers a thread
 stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
               const Params p) {
     constexpr int QT = kRows / G;  // tokens per tile
@@ -285,11 +332,18 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         }
     } else {
         // ------------------------------------------------------------ epilogue
-        const int tid = threadIdx.x;        // 0..255
-        const int wg = warp >> 2;           // which half of the tile
-        const int wq = warp & 3;            // TMEM lane quarter
+        // 16 warps = 4 warpgroups; warp w reads TMEM lanes 32*(w%4)..+31.
+        //   pass 1: warpgroup wg owns accumulator rows (wg>>1)*128.. (one row per
+        //           thread) and key columns (wg&1)*64..+63 of every key tile;
+        //   pass 2: warpgroup wg owns tile rows (= accumulator columns) wg*64..+63,
+        //           i.e. 64/G tokens, and one key per thread.
+        const int tid = threadIdx.x;        // 0..511
+        const int wg = warp >> 2;
+        const int wq = warp & 3;
         const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
         const float c = p.c;
+        const uint64_t c2 = f2_pack(c, c);
+        float2 *part = reinterpret_cast<float2 *>(sgen + kOffPart);  // [2][kRows] (max, sum)
         uint32_t sc = 0;
         for (int64_t w = blockIdx.x; w < n_items; w += gridDim.x) {
             const Item it = decode<QT>(w, p, cu_tiles, n_tiles);
@@ -300,77 +354,108 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
             __nv_bfloat16 *out_g = p.out + (int64_t)it.g * p.T * p.out_stride;
 
             if (it.nkt > 0) {
-                // ---------------- pass 1: softmax statistics of row r = (token, head)
-                const int r = wg * 128 + wq * 32 + lane;
+                // ---------------- pass 1: softmax statistics of row r over this half's keys
+                const int r = (wg >> 1) * 128 + wq * 32 + lane;
                 const int32_t lim_r = lim_s[r / G];
+                const int colh = (wg & 1) * 64;
                 float m = -INFINITY, l = 0.f;
                 for (int32_t kt = 0; kt < it.nkt; ++kt, ++sc) {
                     const uint32_t buf = sc & 1;
                     wait_bar(sy, sy.s_full + 8 * buf, (sc >> 1) & 1, 6);
                     tc_fence_after();
-                    const uint32_t ta = tmem + lane_base + buf * 256 + wg * 128;
-#pragma unroll 1
-                    for (int half = 0; half < 2; ++half) {
-                        float v[64];
-                        tmem_ld32(ta + half * 64, *reinterpret_cast<float(*)[32]>(&v[0]));
-                        tmem_ld32(ta + half * 64 + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
-                        tmem_wait_ld();
-                        const int32_t col0 = kt * kBN + half * 64;
-                        if (col0 + 64 > lim_r) {
-#pragma unroll
-                            for (int i = 0; i < 64; ++i)
-                                if (col0 + i >= lim_r) v[i] = -INFINITY;
-                        }
-                        float mx = v[0];
-#pragma unroll
-                        for (int i = 1; i < 64; ++i) mx = fmaxf(mx, v[i]);
-                        const float m_new = fmaxf(m, mx);
-                        if (m_new != -INFINITY) {
-                            const float mc = m_new * c;
-                            float sum = 0.f;
-#pragma unroll
-                            for (int i = 0; i < 64; ++i) sum += ex2(fmaf(v[i], c, -mc));
-                            l = (m == -INFINITY ? 0.f : l * ex2((m - m_new) * c)) + sum;
-                            m = m_new;
-                        }
-                    }
+                    float v[64];
+                    const uint32_t ta = tmem + lane_base + buf * 256 + (wg >> 1) * 128 + colh;
+                    tmem_ld32(ta, *reinterpret_cast<float(*)[32]>(&v[0]));
+                    tmem_ld32(ta + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+                    tmem_wait_ld();
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(sy.s_empty + 8 * buf);
+                    if (lane == 0) mbar_arrive(sy.s_empty + 8 * buf);  // values are in registers
+                    const int32_t col0 = kt * kBN + colh;
+                    if (col0 + 64 > lim_r) {
+#pragma unroll
+                        for (int i = 0; i < 64; ++i)
+                            if (col0 + i >= lim_r) v[i] = -INFINITY;
+                    }
+                    float mx[3] = {v[0], v[1], v[2]};
+#pragma unroll
+                    for (int i = 3; i + 1 < 63; i += 2) mx[(i >> 1) % 3] = fmax3(mx[(i >> 1) % 3], v[i], v[i + 1]);
+                    const float mt = fmax3(fmax3(mx[0], mx[1], mx[2]), v[63], m);  // running max incl. m
+                    if (mt != -INFINITY) {
+                        const uint64_t nmc = f2_pack(-mt * c, -mt * c);
+                        uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+#define UNUM_P1(P) acc[(P) & 3] = f2_add(acc[(P) & 3], exp2_pair<P>(f2_fma(f2_pack(v[2 * (P)], v[2 * (P) + 1]), c2, nmc)));
+#define UNUM_P1x4(P) UNUM_P1(P) UNUM_P1(P + 1) UNUM_P1(P + 2) UNUM_P1(P + 3)
+                        UNUM_P1x4(0) UNUM_P1x4(4) UNUM_P1x4(8) UNUM_P1x4(12)
+                        UNUM_P1x4(16) UNUM_P1x4(20) UNUM_P1x4(24) UNUM_P1x4(28)
+#undef UNUM_P1x4
+#undef UNUM_P1
+                        const uint64_t a2 = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
+                        float alo, ahi;
+                        f2_unpack(a2, alo, ahi);
+                        l = (m == -INFINITY ? 0.f : l * ex2((m - mt) * c)) + (alo + ahi);
+                        m = mt;
+                    }
                 }
-                stats[r] = (l > 0.f) ? fmaf(m, c, log2f(l)) : INFINITY;
+                part[(wg & 1) * kRows + r] = make_float2(m, l);
+                named_bar_sync(kEpiBarrier, kEpiWarps * 32);
+                if ((wg & 1) == 0) {  // merge the two column halves of row r
+                    const float2 a = part[r], b2 = part[kRows + r];
+                    const float mm = fmaxf(a.x, b2.x);
+                    float ll = 0.f;
+                    if (mm != -INFINITY) {
+                        if (a.x != -INFINITY) ll += a.y * ex2((a.x - mm) * c);
+                        if (b2.x != -INFINITY) ll += b2.y * ex2((b2.x - mm) * c);
+                    }
+                    stats[r] = (ll > 0.f) ? -fmaf(mm, c, log2f(ll)) : -INFINITY;  // -(m*c + log2 l)
+                }
                 named_bar_sync(kEpiBarrier, kEpiWarps * 32);
 
                 // ---------------- pass 2: key j = this thread's TMEM lane
+                constexpr int NQ = 64 / G;  // tokens of this warpgroup
+                const int col0 = wg * 64;   // tile row index of v[0]
+                const int tq0 = col0 / G;
+                const uint64_t *st2 = reinterpret_cast<const uint64_t *>(stats + col0);  // -b, pairwise
                 for (int32_t kt = 0; kt < it.nkt; ++kt, ++sc) {
                     const uint32_t buf = sc & 1;
                     wait_bar(sy, sy.s_full + 8 * buf, (sc >> 1) & 1, 7);
                     tc_fence_after();
-                    const uint32_t ta = tmem + lane_base + buf * 256 + wg * 128;
+                    float v[64];
+                    const uint32_t ta = tmem + lane_base + buf * 256 + col0;
+                    tmem_ld32(ta, *reinterpret_cast<float(*)[32]>(&v[0]));
+                    tmem_ld32(ta + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+                    tmem_wait_ld();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(sy.s_empty + 8 * buf);
                     const int32_t j = kt * kBN + wq * 32 + lane;
-                    const bool j_in_row = j < p.out_stride;
-#pragma unroll 1
-                    for (int ch = 0; ch < 4; ++ch) {
-                        float v[32];
-                        tmem_ld32(ta + ch * 32, v);
-                        tmem_wait_ld();
-                        const int col0 = wg * 128 + ch * 32;  // tile row index of v[0]
+                    uint64_t acc[NQ][2];
 #pragma unroll
-                        for (int qi = 0; qi < 32 / G; ++qi) {
-                            const int tq = (col0 >> __builtin_ctz(G)) + qi;
-                            float acc = 0.f;
+                    for (int qi = 0; qi < NQ; ++qi) acc[qi][0] = acc[qi][1] = 0ull;
+#define UNUM_P2(P)                                                                          \
+    {                                                                                       \
+        const uint64_t x2 = f2_fma(f2_pack(v[2 * (P)], v[2 * (P) + 1]), c2, st2[P]);         \
+        acc[(2 * (P)) / G][(P) & 1] = f2_add(acc[(2 * (P)) / G][(P) & 1], exp2_pair<P>(x2)); \
+    }
+#define UNUM_P2x4(P) UNUM_P2(P) UNUM_P2(P + 1) UNUM_P2(P + 2) UNUM_P2(P + 3)
+                    UNUM_P2x4(0) UNUM_P2x4(4) UNUM_P2x4(8) UNUM_P2x4(12)
+                    UNUM_P2x4(16) UNUM_P2x4(20) UNUM_P2x4(24) UNUM_P2x4(28)
+#undef UNUM_P2x4
+#undef UNUM_P2
+                    if (j < p.out_stride) {
 #pragma unroll
-                            for (int h = 0; h < G; ++h)
-                                acc += ex2(fmaf(v[qi * G + h], c, -stats[col0 + qi * G + h]));
-                            if (tq < it.nq && j_in_row) {
-                                const float o = j < lim_s[tq] ? fmaxf(acc, 0.f) : 0.f;
+                        for (int qi = 0; qi < NQ; ++qi) {
+                            const int tq = tq0 + qi;
+                            if (tq < it.nq) {
+                                float a0, a1, b0, b1;
+                                f2_unpack(acc[qi][0], a0, a1);
+                                f2_unpack(acc[qi][1], b0, b1);
+                                const float a = (a0 + a1) + (b0 + b1);
+                                const float o = j < lim_s[tq] ? fmaxf(a, 0.f) : 0.f;
                                 out_g[(it.t0 + tq) * p.out_stride + j] = __float2bfloat16_rn(o);
                             }
                         }
                     }
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(sy.s_empty + 8 * buf);
                 }
             }
             // ---------------- zero the columns past the computed key tiles
@@ -542,8 +627,8 @@ extern "C" int unum_infllmv2_attn_stage1(const void *q, int64_t T, int64_t Hq, i
         return UNUM_ERR_UNSUPPORTED;
     }
     const int64_t G = Hq / Hk;
-    if (!(G == 1 || G == 2 || G == 4 || G == 8 || G == 16 || G == 32)) {
-        unum::set_error("head group size %lld not supported (1,2,4,8,16,32)", (long long)G);
+    if (!(G == 2 || G == 4 || G == 8 || G == 16 || G == 32)) {
+        unum::set_error("head group size %lld not supported (2,4,8,16,32)", (long long)G);
         return UNUM_ERR_UNSUPPORTED;
     }
     UNUM_CHECK_ARG(out_stride % 128 == 0, "out_stride must be a multiple of 128");
@@ -588,7 +673,6 @@ extern "C" int unum_infllmv2_attn_stage1(const void *q, int64_t T, int64_t Hq, i
     p.causal = causal ? 1 : 0;
     p.c = softmax_scale * kLog2e;
     switch (G) {
-        case 1: return launch_main<1>(mq, mk, p, T, s);
         case 2: return launch_main<2>(mq, mk, p, T, s);
         case 4: return launch_main<4>(mq, mk, p, T, s);
         case 8: return launch_main<8>(mq, mk, p, T, s);

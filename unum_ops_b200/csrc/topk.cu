@@ -9,11 +9,17 @@
 // (test/test_sparse_kernel.py:80-87).
 //
 // B200 design: one warp per row.  The row is staged once in shared memory as
-// order-preserving 32-bit keys (excluded entries get key 0).  A radix select
-// (8-bit digits, a 256-bin warp-private histogram, a warp scan to locate the
-// digit holding the K-th key) finds the threshold key in 2 passes for 16-bit
-// score types and 4 for fp32.  A final ballot/popc sweep in index order emits
-// the winners already sorted, taking only the lowest-index ties.
+// order-preserving keys — 16-bit for bf16/fp16 scores, 32-bit for fp32 —
+// with excluded entries mapped to key 0; 16-byte vector loads from HBM when
+// the rows are aligned.  A radix select (8-bit digits, a 256-bin warp-private
+// histogram, a warp scan to find the digit holding the K-th key) yields the
+// threshold key in 2 passes (16-bit) or 4 (fp32).  Each lane walks 8
+// consecutive keys per step and adds a run of equal digits with one
+// shared-memory atomic, so long runs of equal scores (the zero-score blocks
+// past a causal query) cost one atomic per 8 keys.  The emit sweep walks the
+// row in index order, 8 keys per lane per step, with warp scans for the tie
+// count and the output slot, so winners come out sorted and only the
+// lowest-index ties are taken.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -25,59 +31,116 @@ constexpr int kWarps = 4;
 constexpr int kMaxNB = 4096;
 constexpr int kMaxK = 1024;
 
-template <typename T> __device__ __forceinline__ float to_f(T v);
-template <> __device__ __forceinline__ float to_f<float>(float v) { return v; }
-template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
-template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+// Order-preserving keys: larger score -> larger key; -inf and NaN -> 0.
+template <typename T> struct KeyOf;
+template <> struct KeyOf<float> {
+    using K = uint32_t;
+    static constexpr int kPasses = 4;
+    __device__ static K key(float f) {
+        if (f != f || f == -INFINITY) return 0u;
+        const uint32_t u = __float_as_uint(f);
+        return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    }
+};
+template <> struct KeyOf<__nv_bfloat16> {
+    using K = uint16_t;
+    static constexpr int kPasses = 2;
+    __device__ static K key(__nv_bfloat16 v) {
+        const uint16_t u = __bfloat16_as_ushort(v);
+        if ((u & 0x7F80u) == 0x7F80u && (u & 0x7Fu) != 0) return 0;  // NaN
+        if (u == 0xFF80u) return 0;                                    // -inf
+        return (u & 0x8000u) ? (uint16_t)~u : (uint16_t)(u | 0x8000u);
+    }
+};
+template <> struct KeyOf<__half> {
+    using K = uint16_t;
+    static constexpr int kPasses = 2;
+    __device__ static K key(__half v) {
+        const uint16_t u = __half_as_ushort(v);
+        if ((u & 0x7C00u) == 0x7C00u && (u & 0x3FFu) != 0) return 0;  // NaN
+        if (u == 0xFC00u) return 0;                                     // -inf
+        return (u & 0x8000u) ? (uint16_t)~u : (uint16_t)(u | 0x8000u);
+    }
+};
 
-// Larger score -> larger key; -inf and NaN -> 0 (not a candidate).
-__device__ __forceinline__ uint32_t score_key(float f) {
-    if (f != f || f == -INFINITY) return 0u;
-    uint32_t u = __float_as_uint(f);
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+__device__ __forceinline__ uint32_t warp_incl_scan(uint32_t x, int lane) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t v = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += v;
+    }
+    return x;
 }
 
-template <typename T, int PASSES>
+template <typename T>
 __global__ void __launch_bounds__(kWarps * 32)
-topk_kernel(const T *__restrict__ scores, int64_t rows, int64_t NB, int64_t row_stride, int64_t K,
-            int32_t *__restrict__ out) {
-    extern __shared__ uint32_t smem[];
+topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_stride, int32_t K,
+            bool vec_ok, int32_t *__restrict__ out) {
+    using Key = typename KeyOf<T>::K;
+    constexpr int PASSES = KeyOf<T>::kPasses;
+    constexpr int KB = 8 * (int)sizeof(Key);       // key bits
+    constexpr int VT = 16 / (int)sizeof(T);        // scores per 16-byte load
+    extern __shared__ __align__(16) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint32_t *keys = smem + warp * (NB + 256);
-    uint32_t *hist = keys + NB;
-    const uint32_t lt_mask = (1u << lane) - 1u;
+    const int32_t NBp = (NB + 255) & ~255;         // padded to whole steps (8 keys x 32 lanes)
+    uint32_t *hist = reinterpret_cast<uint32_t *>(smem) + warp * 256;
+    Key *keys = reinterpret_cast<Key *>(smem + kWarps * 256 * 4) + (size_t)warp * NBp;
     for (int64_t row = (int64_t)blockIdx.x * kWarps + warp; row < rows;
          row += (int64_t)gridDim.x * kWarps) {
         const T *src = scores + row * row_stride;
-        for (int64_t i = lane; i < NB; i += 32) keys[i] = score_key(to_f<T>(src[i]));
+        // ---- stage keys (padding keys are 0 = never selected)
+        if (vec_ok) {
+            for (int32_t i = lane * VT; i < NBp; i += 32 * VT) {
+                if (i + VT <= NB) {
+                    const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(src + i));
+                    const T *tv = reinterpret_cast<const T *>(&raw);
+#pragma unroll
+                    for (int e = 0; e < VT; ++e) keys[i + e] = KeyOf<T>::key(tv[e]);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < VT; ++e) keys[i + e] = (i + e < NB) ? KeyOf<T>::key(src[i + e]) : Key(0);
+                }
+            }
+        } else {
+            for (int32_t i = lane; i < NBp; i += 32) keys[i] = i < NB ? KeyOf<T>::key(src[i]) : Key(0);
+        }
+        __syncwarp();
+        // ---- radix select of the K-th largest key
         uint32_t prefix = 0, pmask = 0;
-        int64_t remaining = K;
+        int32_t remaining = K;
         bool take_all = false;
 #pragma unroll 1
         for (int p = 0; p < PASSES; ++p) {
-            const int shift = 24 - 8 * p;
+            const int shift = KB - 8 - 8 * p;
 #pragma unroll
             for (int i = 0; i < 8; ++i) hist[lane * 8 + i] = 0;
             __syncwarp();
-            for (int64_t i = lane; i < NB; i += 32) {
-                const uint32_t k = keys[i];
-                if (k != 0u && (k & pmask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1u);
+            for (int32_t base = 0; base < NBp; base += 256) {
+                const int32_t i0 = base + 8 * lane;
+                uint32_t run_d = 256u, run_c = 0;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const uint32_t k = keys[i0 + e];
+                    const bool m = k != 0u && (k & pmask) == prefix;
+                    const uint32_t d = m ? ((k >> shift) & 255u) : 256u;
+                    if (d != run_d) {
+                        if (run_c) atomicAdd(&hist[run_d], run_c);
+                        run_d = d;
+                        run_c = 0;
+                    }
+                    run_c += m ? 1u : 0u;
+                }
+                if (run_c) atomicAdd(&hist[run_d], run_c);
             }
             __syncwarp();
-            // lane owns bins 255-8*lane-i, i = 0..7 (descending)
             uint32_t c[8];
             uint32_t s = 0;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
+            for (int i = 0; i < 8; ++i) {  // lane owns bins 255-8*lane-i (descending)
                 c[i] = hist[255 - 8 * lane - i];
                 s += c[i];
             }
-            uint32_t incl = s;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += v;
-            }
+            const uint32_t incl = warp_incl_scan(s, lane);
             const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
             if (p == 0 && total <= (uint32_t)K) {
                 take_all = true;
@@ -101,46 +164,71 @@ topk_kernel(const T *__restrict__ scores, int64_t rows, int64_t NB, int64_t row_
             }
             digit = __shfl_sync(0xffffffffu, digit, owner);
             above = __shfl_sync(0xffffffffu, above, owner);
-            remaining -= above;
+            remaining -= (int32_t)above;
             prefix |= digit << shift;
             pmask |= 255u << shift;
             __syncwarp();
         }
-        // emit winners in index order
+        // ---- emit winners in index order: lane takes keys [base + 8*lane, +8)
         int32_t *orow = out + row * K;
-        int64_t pos = 0;
-        int64_t eq_seen = 0;
-        for (int64_t b = 0; b < NB && pos < K; b += 32) {
-            const int64_t i = b + lane;
-            const uint32_t k = i < NB ? keys[i] : 0u;
-            bool sel;
-            if (take_all) {
-                sel = k != 0u;
-            } else {
-                const bool eq = (k == prefix);
-                const uint32_t em = __ballot_sync(0xffffffffu, eq);
-                sel = (k > prefix) || (eq && eq_seen + __popc(em & lt_mask) < remaining);
-                eq_seen += __popc(em);
+        int32_t pos = 0, eq_seen = 0;
+        for (int32_t base = 0; base < NB && pos < K; base += 256) {
+            const int32_t i0 = base + 8 * lane;
+            uint32_t gt = 0, eq = 0;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const uint32_t k = keys[i0 + e];
+                if (take_all) {
+                    gt |= (k != 0u ? 1u : 0u) << e;
+                } else {
+                    gt |= (k > prefix ? 1u : 0u) << e;
+                    eq |= (k == prefix ? 1u : 0u) << e;
+                }
             }
-            const uint32_t sm = __ballot_sync(0xffffffffu, sel);
-            if (sel) orow[pos + __popc(sm & lt_mask)] = (int32_t)i;
-            pos += __popc(sm);
+            const uint32_t ne = (uint32_t)__popc(eq);
+            const uint32_t eincl = warp_incl_scan(ne, lane);
+            // ties taken: the first `remaining - eq_seen` ties of this row, in index order
+            int32_t eq_budget = remaining - eq_seen - (int32_t)(eincl - ne);
+            uint32_t sel = gt;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                if ((eq >> e) & 1u) {
+                    if (eq_budget > 0) sel |= 1u << e;
+                    --eq_budget;
+                }
+            }
+            const uint32_t nsel = (uint32_t)__popc(sel);
+            const uint32_t si = warp_incl_scan(nsel, lane);
+            int32_t slot = pos + (int32_t)(si - nsel);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                if ((sel >> e) & 1u) {
+                    if (slot < K) orow[slot] = i0 + e;
+                    ++slot;
+                }
+            }
+            pos += (int32_t)__shfl_sync(0xffffffffu, si, 31);
+            eq_seen += (int32_t)__shfl_sync(0xffffffffu, eincl, 31);
         }
-        for (int64_t s2 = pos + lane; s2 < K; s2 += 32) orow[s2] = -1;
+        for (int32_t s2 = (pos < K ? pos : K) + lane; s2 < K; s2 += 32) orow[s2] = -1;
         __syncwarp();
     }
 }
 
-template <typename T, int PASSES>
+template <typename T>
 int launch_topk(const void *scores, int64_t rows, int64_t NB, int64_t row_stride, int64_t K,
                 int32_t *out, cudaStream_t s) {
-    const size_t smem = (size_t)kWarps * (NB + 256) * sizeof(uint32_t);
-    auto kern = topk_kernel<T, PASSES>;
+    using Key = typename KeyOf<T>::K;
+    const int64_t NBp = (NB + 255) & ~(int64_t)255;
+    const size_t smem = (size_t)kWarps * (256 * 4 + NBp * sizeof(Key));
+    auto kern = topk_kernel<T>;
     UNUM_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const int64_t want = (rows + kWarps - 1) / kWarps;
     const int64_t cap = (int64_t)unum::sm_count() * 64;
     const int grid = (int)(want < cap ? want : cap);
-    kern<<<grid, kWarps * 32, smem, s>>>((const T *)scores, rows, NB, row_stride, K, out);
+    const bool vec_ok = unum::aligned16(scores) && ((row_stride * (int64_t)sizeof(T)) % 16 == 0);
+    kern<<<grid, kWarps * 32, smem, s>>>((const T *)scores, rows, (int32_t)NB, row_stride, (int32_t)K,
+                                         vec_ok, out);
     return unum::check_launch("topk_kernel");
 }
 
@@ -161,9 +249,9 @@ extern "C" int unum_topk_blocks(const void *scores, int dtype, int64_t rows, int
         return UNUM_OK;
     }
     switch (dtype) {
-        case UNUM_DTYPE_F32: return launch_topk<float, 4>(scores, rows, NB, row_stride, K, out, s);
-        case UNUM_DTYPE_BF16: return launch_topk<__nv_bfloat16, 2>(scores, rows, NB, row_stride, K, out, s);
-        case UNUM_DTYPE_F16: return launch_topk<__half, 2>(scores, rows, NB, row_stride, K, out, s);
+        case UNUM_DTYPE_F32: return launch_topk<float>(scores, rows, NB, row_stride, K, out, s);
+        case UNUM_DTYPE_BF16: return launch_topk<__nv_bfloat16>(scores, rows, NB, row_stride, K, out, s);
+        case UNUM_DTYPE_F16: return launch_topk<__half>(scores, rows, NB, row_stride, K, out, s);
         default:
             unum::set_error("unsupported dtype %d", dtype);
             return UNUM_ERR_UNSUPPORTED;
