@@ -151,6 +151,30 @@ int unum_infllmv2_attn_stage1(const void *q, int64_t T, int64_t Hq, int64_t D, i
  */
 int unum_stage1_status(const void *workspace, void *stream, int32_t *status_out);
 
+/*
+ * infllmv2_attn_stage1_noalloc — unum_infllmv2_attn_stage1 without a workspace.
+ * No counterpart in the reference: an addition of this library for callers
+ * that cannot allocate device memory when they run stage 1 (an engine whose
+ * allocator already owns all of HBM, a plugin host that forbids cudaMalloc in
+ * its callbacks).  The schedule scratch is a fixed 64 KB array inside the
+ * library, held by every GPU that loads the library until the process exits.
+ *
+ * Same arguments and results as unum_infllmv2_attn_stage1, minus the
+ * workspace.  Limit: n_seq <= 16379 (larger batches fail with
+ * UNUM_ERR_INVALID and a message).  Runs on the current device; the first
+ * call on each device looks up the array's device address
+ * (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * The call allocates nothing.  All calls on a device share the one array and
+ * every call rewrites it fully, so calls that overlap on the GPU (different
+ * streams, no ordering between them) race and must be avoided.
+ */
+int unum_infllmv2_attn_stage1_noalloc(const void *q, int64_t T, int64_t Hq, int64_t D,
+                                      int64_t q_st, int64_t q_sh, const void *k, int64_t Tk,
+                                      int64_t Hk, int64_t k_st, int64_t k_sh,
+                                      const int32_t *cu_seqlens_q, const int32_t *cu_seqlens_k,
+                                      int64_t n_seq, float softmax_scale, int causal, void *out,
+                                      int64_t out_stride, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

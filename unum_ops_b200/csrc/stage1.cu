@@ -689,3 +689,67 @@ extern "C" int unum_stage1_status(const void *workspace, void *stream, int32_t *
     UNUM_CHECK_CUDA(cudaStreamSynchronize(s));
     return UNUM_OK;
 }
+
+// ------------------------------------------------------------------ allocation-free variant
+// Some callers cannot allocate device memory at the point where they run
+// stage 1: an inference engine whose allocator has carved up all of HBM up
+// front, a plugin host that forbids cudaMalloc inside its callbacks, or code
+// running where an allocation would synchronise the device.  For them the
+// schedule scratch lives in this fixed, library-owned array instead of a
+// caller-supplied workspace.  Every GPU that loads the library keeps it
+// (64 KB) until the process exits.
+#include <mutex>
+
+namespace {
+
+constexpr int64_t kNoAllocMaxSeqs = 16379;  // (4 + 16379 + 1) * 4 bytes = the whole array
+constexpr size_t kNoAllocBytes = 65536;
+static __device__ __align__(256) int32_t g_stage1_scratch[kNoAllocBytes / 4];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void *g_scratch_ptr[kMaxDevices] = {nullptr};
+
+// Device address of g_stage1_scratch on the current device (looked up once per
+// device; host code cannot use the symbol itself as a device pointer).
+int scratch_for_current_device(void **out) {
+    int dev = 0;
+    UNUM_CHECK_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) {
+        unum::set_error("device index %d out of range", dev);
+        return UNUM_ERR_INVALID;
+    }
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_ptr[dev]) {
+        void *p = nullptr;
+        UNUM_CHECK_CUDA(cudaGetSymbolAddress(&p, g_stage1_scratch));
+        g_scratch_ptr[dev] = p;
+    }
+    *out = g_scratch_ptr[dev];
+    return UNUM_OK;
+}
+
+}  // namespace
+
+extern "C" int unum_infllmv2_attn_stage1_noalloc(const void *q, int64_t T, int64_t Hq, int64_t D,
+                                                 int64_t q_st, int64_t q_sh, const void *k,
+                                                 int64_t Tk, int64_t Hk, int64_t k_st, int64_t k_sh,
+                                                 const int32_t *cu_seqlens_q,
+                                                 const int32_t *cu_seqlens_k, int64_t n_seq,
+                                                 float softmax_scale, int causal, void *out,
+                                                 int64_t out_stride, void *stream) {
+    unum::clear_error();
+    if (n_seq < 0 || n_seq > kNoAllocMaxSeqs) {
+        unum::set_error("unum_infllmv2_attn_stage1_noalloc supports at most %lld sequences per "
+                        "call (got %lld); use unum_infllmv2_attn_stage1 with a workspace",
+                        (long long)kNoAllocMaxSeqs, (long long)n_seq);
+        return UNUM_ERR_INVALID;
+    }
+    void *scratch = nullptr;
+    if (int rc = scratch_for_current_device(&scratch)) return rc;
+    // The prologue kernel rewrites the status word and the whole tile prefix
+    // on every call, so nothing left from an earlier call is read.
+    return unum_infllmv2_attn_stage1(q, T, Hq, D, q_st, q_sh, k, Tk, Hk, k_st, k_sh, cu_seqlens_q,
+                                     cu_seqlens_k, n_seq, softmax_scale, causal, out, out_stride,
+                                     scratch, kNoAllocBytes, stream);
+}
