@@ -69,7 +69,12 @@ constexpr uint32_t kOffLim = kOffPart + 2 * kRows * 8;
 constexpr uint32_t kOffBar = kOffLim + kRows * 4;
 constexpr uint32_t kNumBars = 2 + 2 * kStages + 4;
 constexpr uint32_t kOffMisc = kOffBar + kNumBars * 8;
-constexpr uint32_t kSmemBytes = kOffMisc + 64 + 1024;  // + slack for 1024-byte alignment
+constexpr uint32_t kOffStage = (kOffMisc + 64 + 1023) & ~1023u;  // pass-2 output staging (TMA needs 128-B alignment)
+constexpr uint32_t kStageWg = 1024;                        // one [NQ=4 x 128] bf16 tile (G >= 16)
+constexpr uint32_t kStageBytes = 4 * 2 * kStageWg;         // 4 warpgroups x 2 buffers
+constexpr uint32_t kSmemBytes = kOffStage + kStageBytes + 1024;  // + slack for 1024-byte alignment
+static_assert(kOffStage % 128 == 0 && kStageWg % 128 == 0, "TMA store sources must be 128-byte aligned");
+static_assert(kSmemBytes <= 232448, "exceeds the 227 KB of shared memory a CTA may use");
 
 constexpr uint32_t kIdescP1 = idesc_bf16_f32(128, 128);
 constexpr uint32_t kIdescP2 = idesc_bf16_f32(128, 256);
@@ -143,7 +148,7 @@ __device__ __forceinline__ uint64_t exp2_mufu2(uint64_t x2) {
 
 // Pair p of a 64-value strip uses the polynomial when p % kPolyMod == kPolyMod-1.
 #ifndef UNUM_POLY_MOD
-#define UNUM_POLY_MOD 4
+#define UNUM_POLY_MOD 0
 #endif
 constexpr int kPolyMod = UNUM_POLY_MOD;
 template <int P>
@@ -202,10 +207,59 @@ __device__ __forceinline__ bool wait_bar(const Sync &s, uint32_t bar, uint32_t p
     }
 }
 
+// ---------------------------------------------------------------- epilogue pieces
+// Pass 1 on 32 columns of row r: fold them into the running (max m, sum l).
+__device__ __forceinline__ void p1_chunk(float (&v)[32], int32_t colbase, int32_t lim_r, float c,
+                                         uint64_t c2, float &m, float &l) {
+    if (colbase + 32 > lim_r) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (colbase + i >= lim_r) v[i] = -INFINITY;
+    }
+    float mx[3] = {v[0], v[1], v[2]};
+#pragma unroll
+    for (int i = 3; i + 1 < 31; i += 2) mx[(i >> 1) % 3] = fmax3(mx[(i >> 1) % 3], v[i], v[i + 1]);
+    const float mt = fmax3(fmax3(mx[0], mx[1], mx[2]), v[31], m);  // new running max
+    if (mt == -INFINITY) return;
+    const uint64_t nmc = f2_pack(-mt * c, -mt * c);
+    uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+#define UNUM_P1(P) acc[(P) & 3] = f2_add(acc[(P) & 3], exp2_pair<P>(f2_fma(f2_pack(v[2 * (P)], v[2 * (P) + 1]), c2, nmc)));
+#define UNUM_P1x4(P) UNUM_P1(P) UNUM_P1(P + 1) UNUM_P1(P + 2) UNUM_P1(P + 3)
+    UNUM_P1x4(0) UNUM_P1x4(4) UNUM_P1x4(8) UNUM_P1x4(12)
+#undef UNUM_P1x4
+#undef UNUM_P1
+    const uint64_t a2 = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
+    float alo, ahi;
+    f2_unpack(a2, alo, ahi);
+    if (mt != m) l = (m == -INFINITY ? 0.f : l * ex2((m - mt) * c));  // rescale only when the max moved
+    l += alo + ahi;
+    m = mt;
+}
+
+// Pass 2 on accumulator columns H*32..H*32+31 of this warpgroup (key = TMEM lane):
+// add exp2(s*c - b) into the per-token head sums.
+template <int G, int H>
+__device__ __forceinline__ void p2_chunk(const float (&v)[32], uint64_t (&acc)[64 / G][2],
+                                         const ulonglong2 *st4, uint64_t c2) {
+#define UNUM_P2(P, SV)                                                                              \
+    {                                                                                               \
+        const uint64_t x2 = f2_fma(f2_pack(v[2 * (P)], v[2 * (P) + 1]), c2, SV);                    \
+        acc[(H * 32 + 2 * (P)) / G][(P) & 1] = f2_add(acc[(H * 32 + 2 * (P)) / G][(P) & 1], exp2_pair<P>(x2)); \
+    }
+#define UNUM_P2x2(P)                                                                                \
+    {                                                                                               \
+        const ulonglong2 sv = st4[H * 8 + ((P) >> 1)]; /* two pairs of -b per shared load */        \
+        UNUM_P2(P, sv.x) UNUM_P2(P + 1, sv.y)                                                       \
+    }
+    UNUM_P2x2(0) UNUM_P2x2(2) UNUM_P2x2(4) UNUM_P2x2(6) UNUM_P2x2(8) UNUM_P2x2(10) UNUM_P2x2(12) UNUM_P2x2(14)
+#undef UNUM_P2x2
+#undef UNUM_P2
+}
+
 template <int G>
 __global__ void __launch_bounds__(kThreads, 1)  // 18 warps: at most 96 registers a thread
 stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-              const Params p) {
+              const __grid_constant__ CUtensorMap tmO, const Params p) {
     constexpr int QT = kRows / G;  // tokens per tile
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -344,7 +398,7 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         const float c = p.c;
         const uint64_t c2 = f2_pack(c, c);
         float2 *part = reinterpret_cast<float2 *>(sgen + kOffPart);  // [2][kRows] (max, sum)
-        uint32_t sc = 0;
+        uint32_t sc = 0, stc = 0;
         for (int64_t w = blockIdx.x; w < n_items; w += gridDim.x) {
             const Item it = decode<QT>(w, p, cu_tiles, n_tiles);
             named_bar_sync(kEpiBarrier, kEpiWarps * 32);  // previous tile done with lim_s/stats
@@ -359,43 +413,20 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                 const int32_t lim_r = lim_s[r / G];
                 const int colh = (wg & 1) * 64;
                 float m = -INFINITY, l = 0.f;
+                const uint32_t tcol = lane_base + (wg >> 1) * 128 + colh;
                 for (int32_t kt = 0; kt < it.nkt; ++kt, ++sc) {
                     const uint32_t buf = sc & 1;
                     wait_bar(sy, sy.s_full + 8 * buf, (sc >> 1) & 1, 6);
                     tc_fence_after();
-                    float v[64];
-                    const uint32_t ta = tmem + lane_base + buf * 256 + (wg >> 1) * 128 + colh;
-                    tmem_ld32(ta, *reinterpret_cast<float(*)[32]>(&v[0]));
-                    tmem_ld32(ta + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+                    float va[32], vb[32];
+                    tmem_ld32(tmem + tcol + buf * 256, va);
+                    tmem_ld32(tmem + tcol + buf * 256 + 32, vb);
                     tmem_wait_ld();
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(sy.s_empty + 8 * buf);  // values are in registers
-                    const int32_t col0 = kt * kBN + colh;
-                    if (col0 + 64 > lim_r) {
-#pragma unroll
-                        for (int i = 0; i < 64; ++i)
-                            if (col0 + i >= lim_r) v[i] = -INFINITY;
-                    }
-                    float mx[3] = {v[0], v[1], v[2]};
-#pragma unroll
-                    for (int i = 3; i + 1 < 63; i += 2) mx[(i >> 1) % 3] = fmax3(mx[(i >> 1) % 3], v[i], v[i + 1]);
-                    const float mt = fmax3(fmax3(mx[0], mx[1], mx[2]), v[63], m);  // running max incl. m
-                    if (mt != -INFINITY) {
-                        const uint64_t nmc = f2_pack(-mt * c, -mt * c);
-                        uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
-#define UNUM_P1(P) acc[(P) & 3] = f2_add(acc[(P) & 3], exp2_pair<P>(f2_fma(f2_pack(v[2 * (P)], v[2 * (P) + 1]), c2, nmc)));
-#define UNUM_P1x4(P) UNUM_P1(P) UNUM_P1(P + 1) UNUM_P1(P + 2) UNUM_P1(P + 3)
-                        UNUM_P1x4(0) UNUM_P1x4(4) UNUM_P1x4(8) UNUM_P1x4(12)
-                        UNUM_P1x4(16) UNUM_P1x4(20) UNUM_P1x4(24) UNUM_P1x4(28)
-#undef UNUM_P1x4
-#undef UNUM_P1
-                        const uint64_t a2 = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
-                        float alo, ahi;
-                        f2_unpack(a2, alo, ahi);
-                        l = (m == -INFINITY ? 0.f : l * ex2((m - mt) * c)) + (alo + ahi);
-                        m = mt;
-                    }
+                    p1_chunk(va, kt * kBN + colh, lim_r, c, c2, m, l);
+                    p1_chunk(vb, kt * kBN + colh + 32, lim_r, c, c2, m, l);
                 }
                 part[(wg & 1) * kRows + r] = make_float2(m, l);
                 named_bar_sync(kEpiBarrier, kEpiWarps * 32);
@@ -413,36 +444,52 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
 
                 // ---------------- pass 2: key j = this thread's TMEM lane
                 constexpr int NQ = 64 / G;  // tokens of this warpgroup
+                constexpr bool kTmaStore = (G >= 16);  // staging fits [NQ x 128] bf16 in kStageWg
                 const int col0 = wg * 64;   // tile row index of v[0]
                 const int tq0 = col0 / G;
-                const uint64_t *st2 = reinterpret_cast<const uint64_t *>(stats + col0);  // -b, pairwise
+                const ulonglong2 *st4 = reinterpret_cast<const ulonglong2 *>(stats + col0);  // -b, 4 at a time
+                const uint32_t tcol2 = lane_base + col0;
                 for (int32_t kt = 0; kt < it.nkt; ++kt, ++sc) {
                     const uint32_t buf = sc & 1;
+                    const int32_t j = kt * kBN + wq * 32 + lane;
                     wait_bar(sy, sy.s_full + 8 * buf, (sc >> 1) & 1, 7);
                     tc_fence_after();
-                    float v[64];
-                    const uint32_t ta = tmem + lane_base + buf * 256 + col0;
-                    tmem_ld32(ta, *reinterpret_cast<float(*)[32]>(&v[0]));
-                    tmem_ld32(ta + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+                    float wa[32], wb[32];
+                    tmem_ld32(tmem + tcol2 + buf * 256, wa);
+                    tmem_ld32(tmem + tcol2 + buf * 256 + 32, wb);
                     tmem_wait_ld();
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(sy.s_empty + 8 * buf);
-                    const int32_t j = kt * kBN + wq * 32 + lane;
                     uint64_t acc[NQ][2];
 #pragma unroll
                     for (int qi = 0; qi < NQ; ++qi) acc[qi][0] = acc[qi][1] = 0ull;
-#define UNUM_P2(P)                                                                          \
-    {                                                                                       \
-        const uint64_t x2 = f2_fma(f2_pack(v[2 * (P)], v[2 * (P) + 1]), c2, st2[P]);         \
-        acc[(2 * (P)) / G][(P) & 1] = f2_add(acc[(2 * (P)) / G][(P) & 1], exp2_pair<P>(x2)); \
-    }
-#define UNUM_P2x4(P) UNUM_P2(P) UNUM_P2(P + 1) UNUM_P2(P + 2) UNUM_P2(P + 3)
-                    UNUM_P2x4(0) UNUM_P2x4(4) UNUM_P2x4(8) UNUM_P2x4(12)
-                    UNUM_P2x4(16) UNUM_P2x4(20) UNUM_P2x4(24) UNUM_P2x4(28)
-#undef UNUM_P2x4
-#undef UNUM_P2
-                    if (j < p.out_stride) {
+                    p2_chunk<G, 0>(wa, acc, st4, c2);
+                    p2_chunk<G, 1>(wb, acc, st4, c2);
+                    if (kTmaStore && tq0 + NQ <= it.nq) {
+                        // stage the warpgroup's [NQ tokens x 128 keys] tile, then one TMA store
+                        const uint32_t buf_s = stc & 1;
+                        __nv_bfloat16 *stg = reinterpret_cast<__nv_bfloat16 *>(
+                            sgen + kOffStage + (wg * 2 + buf_s) * kStageWg);
+#pragma unroll
+                        for (int qi = 0; qi < NQ; ++qi) {
+                            float a0, a1, b0, b1;
+                            f2_unpack(acc[qi][0], a0, a1);
+                            f2_unpack(acc[qi][1], b0, b1);
+                            const float a = (a0 + a1) + (b0 + b1);
+                            const float o = j < lim_s[tq0 + qi] ? fmaxf(a, 0.f) : 0.f;
+                            stg[qi * kBN + wq * 32 + lane] = __float2bfloat16_rn(o);
+                        }
+                        fence_async_shared();
+                        if (wq == 0 && lane == 0) bulk_wait_read_all();  // previous store left its buffer
+                        named_bar_sync(2 + wg, 128);
+                        if (wq == 0 && lane == 0) {
+                            tma_store_2d(&tmO, smem_u32(stg), kt * kBN,
+                                         (int32_t)((int64_t)it.g * p.T + it.t0 + tq0));
+                            bulk_commit();
+                        }
+                        ++stc;
+                    } else if (j < p.out_stride) {
 #pragma unroll
                         for (int qi = 0; qi < NQ; ++qi) {
                             const int tq = tq0 + qi;
@@ -474,6 +521,7 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                 }
             }
         }
+        if (wq == 0 && lane == 0) bulk_wait_all();  // output stores complete before exit
     }
 
     tc_fence_before();
@@ -590,15 +638,15 @@ int make_map(CUtensorMap *m, const void *base, uint64_t dim0, uint64_t dim1, uin
 }
 
 template <int G>
-int launch_main(const CUtensorMap &mq, const CUtensorMap &mk, const Params &p, int64_t T,
-                cudaStream_t s) {
+int launch_main(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mo,
+                const Params &p, int64_t T, cudaStream_t s) {
     auto kern = stage1_kernel<G>;
     UNUM_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     constexpr int QT = kRows / G;
     const int64_t items_ub = ((T + QT - 1) / QT + p.n_seq) * p.Hk;
     const int64_t sms = unum::sm_count();
     const int grid = (int)(items_ub < sms ? items_ub : sms);
-    kern<<<grid, kThreads, kSmemBytes, s>>>(mq, mk, p);
+    kern<<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mo, p);
     return unum::check_launch("stage1_kernel");
 }
 
@@ -661,6 +709,21 @@ extern "C" int unum_infllmv2_attn_stage1(const void *q, int64_t T, int64_t Hq, i
     if (int rc = make_map(&mk, k, (uint64_t)D, (uint64_t)Hk, (uint64_t)Tk, (uint64_t)k_sh * 2,
                           (uint64_t)k_st * 2, 1, kBN))
         return rc;
+    CUtensorMap mo;  // out as a 2-D [Hk*T, out_stride] bf16 tensor, [64/G x 128] store boxes
+    {
+        auto enc = get_encode_fn();
+        cuuint64_t gdim[2] = {(cuuint64_t)out_stride, (cuuint64_t)(Hk * T)};
+        cuuint64_t gstride[1] = {(cuuint64_t)out_stride * 2};
+        cuuint32_t box[2] = {kBN, (cuuint32_t)(64 / G)};
+        cuuint32_t estr[2] = {1, 1};
+        CUresult r = enc(&mo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, gdim, gstride, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            unum::set_error("cuTensorMapEncodeTiled (out) failed (%d)", (int)r);
+            return UNUM_ERR_CUDA;
+        }
+    }
     Params p;
     p.cu_q = cu_seqlens_q;
     p.cu_k = cu_seqlens_k;
@@ -673,11 +736,11 @@ extern "C" int unum_infllmv2_attn_stage1(const void *q, int64_t T, int64_t Hq, i
     p.causal = causal ? 1 : 0;
     p.c = softmax_scale * kLog2e;
     switch (G) {
-        case 2: return launch_main<2>(mq, mk, p, T, s);
-        case 4: return launch_main<4>(mq, mk, p, T, s);
-        case 8: return launch_main<8>(mq, mk, p, T, s);
-        case 16: return launch_main<16>(mq, mk, p, T, s);
-        default: return launch_main<32>(mq, mk, p, T, s);
+        case 2: return launch_main<2>(mq, mk, mo, p, T, s);
+        case 4: return launch_main<4>(mq, mk, mo, p, T, s);
+        case 8: return launch_main<8>(mq, mk, mo, p, T, s);
+        case 16: return launch_main<16>(mq, mk, mo, p, T, s);
+        default: return launch_main<32>(mq, mk, mo, p, T, s);
     }
 }
 

@@ -1,0 +1,71 @@
+"""Work partitioning of the block-selection path across GPUs (one process per GPU).
+
+The path has no exchange step: sequences are independent, and so are
+(kv head, query range) pieces of one long sequence.  These planners decide
+which rank computes what; each rank then runs the ordinary kernels on its
+shard and results are gathered only if the caller needs them in one place.
+
+* ``plan_sequences``: longest-processing-time bin packing of whole sequences
+  onto ranks by their stage-1 work (visible query/key pairs), for varlen
+  prefill and decode batches.
+* ``plan_query_ranges``: split one causal sequence into query ranges of equal
+  stage-1 work (causal rows grow linearly, so equal row counts would be
+  unbalanced by up to 2x).
+"""
+from __future__ import annotations
+
+import heapq
+
+import numpy as np
+
+
+def visible_counts(q_len: int, k_len: int, causal: bool = True) -> np.ndarray:
+    """Visible compressed keys per query (C integer division, like the kernels)."""
+    lq = np.arange(q_len, dtype=np.int64)
+    if not causal:
+        return np.full(q_len, max(k_len, 0), np.int64)
+    off = np.trunc((lq - 15) / 16).astype(np.int64) + k_len - int(np.trunc((q_len - 15) / 16))
+    return np.clip(off, 0, max(k_len, 0))
+
+
+def sequence_cost(q_lens, k_lens, causal: bool = True) -> np.ndarray:
+    """Stage-1 work of each sequence: visible (query, key) pairs plus one per query."""
+    return np.array([int(visible_counts(q, k, causal).sum()) + q for q, k in zip(q_lens, k_lens)],
+                    np.int64)
+
+
+def plan_sequences(costs, n_ranks: int) -> list[list[int]]:
+    """Assign sequence indices to ranks, largest first onto the least-loaded rank.
+
+    Returns one sorted index list per rank; every index appears exactly once.
+    """
+    if n_ranks <= 0:
+        raise ValueError("n_ranks must be positive")
+    heap = [(0, r) for r in range(n_ranks)]
+    out: list[list[int]] = [[] for _ in range(n_ranks)]
+    for i in sorted(range(len(costs)), key=lambda i: (-int(costs[i]), i)):
+        load, r = heapq.heappop(heap)
+        out[r].append(i)
+        heapq.heappush(heap, (load + int(costs[i]), r))
+    return [sorted(x) for x in out]
+
+
+def plan_query_ranges(q_len: int, k_len: int, n_parts: int, causal: bool = True,
+                      align: int = 64) -> list[tuple[int, int]]:
+    """Split [0, q_len) into n_parts contiguous ranges of near-equal stage-1 work.
+
+    Boundaries are multiples of ``align`` (a 64-token sparse block, so pooling's
+    local-window rows never straddle shards) except the last.
+    """
+    if n_parts <= 0:
+        raise ValueError("n_parts must be positive")
+    w = visible_counts(q_len, k_len, causal) + 1
+    cum = np.concatenate([[0], np.cumsum(w)])
+    total = cum[-1]
+    bounds = [0]
+    for i in range(1, n_parts):
+        t = int(np.searchsorted(cum, total * i / n_parts))
+        t = int(round(t / align)) * align
+        bounds.append(min(max(t, bounds[-1]), q_len))
+    bounds.append(q_len)
+    return [(bounds[i], bounds[i + 1]) for i in range(n_parts)]
