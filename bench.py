@@ -184,6 +184,7 @@ def run_ours(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep rank 0's stdout to the one JSON line
         dist.init_process_group("nccl", device_id=dev)
     unum_ops_b200.load()
 

@@ -146,15 +146,18 @@ __device__ __forceinline__ uint64_t exp2_mufu2(uint64_t x2) {
     return f2_pack(ex2(lo), ex2(hi));
 }
 
-// Pair p of a 64-value strip uses the polynomial when p % kPolyMod == kPolyMod-1.
-#ifndef UNUM_POLY_MOD
-#define UNUM_POLY_MOD 0
+// Pair p of a strip uses the polynomial when p % mod == mod-1 (mod 0: never);
+// pass 1 and pass 2 have their own share.
+#ifndef UNUM_POLY_MOD1
+#define UNUM_POLY_MOD1 0
 #endif
-constexpr int kPolyMod = UNUM_POLY_MOD;
-template <int P>
-__device__ __forceinline__ uint64_t exp2_pair(uint64_t x2) {
-    return (kPolyMod > 0 && P % (kPolyMod > 0 ? kPolyMod : 1) == kPolyMod - 1) ? exp2_fma2(x2)
-                                                                               : exp2_mufu2(x2);
+#ifndef UNUM_POLY_MOD2
+#define UNUM_POLY_MOD2 0
+#endif
+template <int MOD, int P>
+__device__ __forceinline__ uint64_t exp2_pair_mod(uint64_t x2) {
+    if constexpr (MOD > 0 && P % (MOD > 0 ? MOD : 1) == MOD - 1) return exp2_fma2(x2);
+    else return exp2_mufu2(x2);
 }
 
 template <int QT>
@@ -208,24 +211,26 @@ __device__ __forceinline__ bool wait_bar(const Sync &s, uint32_t bar, uint32_t p
 }
 
 // ---------------------------------------------------------------- epilogue pieces
-// Pass 1 on 32 columns of row r: fold them into the running (max m, sum l).
-__device__ __forceinline__ void p1_chunk(float (&v)[32], int32_t colbase, int32_t lim_r, float c,
+// Pass 1 on N (32 or 64) columns of row r: fold them into the running (max m, sum l).
+template <int N>
+__device__ __forceinline__ void p1_chunk(float (&v)[N], int32_t colbase, int32_t lim_r, float c,
                                          uint64_t c2, float &m, float &l) {
-    if (colbase + 32 > lim_r) {
+    if (colbase + N > lim_r) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
+        for (int i = 0; i < N; ++i)
             if (colbase + i >= lim_r) v[i] = -INFINITY;
     }
     float mx[3] = {v[0], v[1], v[2]};
 #pragma unroll
-    for (int i = 3; i + 1 < 31; i += 2) mx[(i >> 1) % 3] = fmax3(mx[(i >> 1) % 3], v[i], v[i + 1]);
-    const float mt = fmax3(fmax3(mx[0], mx[1], mx[2]), v[31], m);  // new running max
+    for (int i = 3; i + 1 < N - 1; i += 2) mx[(i >> 1) % 3] = fmax3(mx[(i >> 1) % 3], v[i], v[i + 1]);
+    const float mt = fmax3(fmax3(mx[0], mx[1], mx[2]), v[N - 1], m);  // new running max
     if (mt == -INFINITY) return;
     const uint64_t nmc = f2_pack(-mt * c, -mt * c);
     uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
-#define UNUM_P1(P) acc[(P) & 3] = f2_add(acc[(P) & 3], exp2_pair<P>(f2_fma(f2_pack(v[2 * (P)], v[2 * (P) + 1]), c2, nmc)));
+#define UNUM_P1(P) if ((P) < N / 2) acc[(P) & 3] = f2_add(acc[(P) & 3], exp2_pair_mod<UNUM_POLY_MOD1, P>(f2_fma(f2_pack(v[2 * (P)], v[2 * (P) + 1]), c2, nmc)));
 #define UNUM_P1x4(P) UNUM_P1(P) UNUM_P1(P + 1) UNUM_P1(P + 2) UNUM_P1(P + 3)
     UNUM_P1x4(0) UNUM_P1x4(4) UNUM_P1x4(8) UNUM_P1x4(12)
+    UNUM_P1x4(16) UNUM_P1x4(20) UNUM_P1x4(24) UNUM_P1x4(28)
 #undef UNUM_P1x4
 #undef UNUM_P1
     const uint64_t a2 = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
@@ -244,7 +249,7 @@ __device__ __forceinline__ void p2_chunk(const float (&v)[32], uint64_t (&acc)[6
 #define UNUM_P2(P, SV)                                                                              \
     {                                                                                               \
         const uint64_t x2 = f2_fma(f2_pack(v[2 * (P)], v[2 * (P) + 1]), c2, SV);                    \
-        acc[(H * 32 + 2 * (P)) / G][(P) & 1] = f2_add(acc[(H * 32 + 2 * (P)) / G][(P) & 1], exp2_pair<P>(x2)); \
+        acc[(H * 32 + 2 * (P)) / G][(P) & 1] = f2_add(acc[(H * 32 + 2 * (P)) / G][(P) & 1], exp2_pair_mod<UNUM_POLY_MOD2, H * 16 + (P)>(x2)); \
     }
 #define UNUM_P2x2(P)                                                                                \
     {                                                                                               \
@@ -418,15 +423,19 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                     const uint32_t buf = sc & 1;
                     wait_bar(sy, sy.s_full + 8 * buf, (sc >> 1) & 1, 6);
                     tc_fence_after();
-                    float va[32], vb[32];
-                    tmem_ld32(tmem + tcol + buf * 256, va);
-                    tmem_ld32(tmem + tcol + buf * 256 + 32, vb);
+                    float v64[64];
+#if UNUM_LD64
+                    tmem_ld64(tmem + tcol + buf * 256, v64);
+#else
+                    tmem_ld32(tmem + tcol + buf * 256, *reinterpret_cast<float(*)[32]>(&v64[0]));
+                    tmem_ld32(tmem + tcol + buf * 256 + 32, *reinterpret_cast<float(*)[32]>(&v64[32]));
+#endif
+
                     tmem_wait_ld();
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(sy.s_empty + 8 * buf);  // values are in registers
-                    p1_chunk(va, kt * kBN + colh, lim_r, c, c2, m, l);
-                    p1_chunk(vb, kt * kBN + colh + 32, lim_r, c, c2, m, l);
+                    p1_chunk<64>(v64, kt * kBN + colh, lim_r, c, c2, m, l);
                 }
                 part[(wg & 1) * kRows + r] = make_float2(m, l);
                 named_bar_sync(kEpiBarrier, kEpiWarps * 32);
@@ -454,9 +463,15 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                     const int32_t j = kt * kBN + wq * 32 + lane;
                     wait_bar(sy, sy.s_full + 8 * buf, (sc >> 1) & 1, 7);
                     tc_fence_after();
-                    float wa[32], wb[32];
-                    tmem_ld32(tmem + tcol2 + buf * 256, wa);
-                    tmem_ld32(tmem + tcol2 + buf * 256 + 32, wb);
+                    float w64[64];
+#if UNUM_LD64
+                    tmem_ld64(tmem + tcol2 + buf * 256, w64);
+#else
+                    tmem_ld32(tmem + tcol2 + buf * 256, *reinterpret_cast<float(*)[32]>(&w64[0]));
+                    tmem_ld32(tmem + tcol2 + buf * 256 + 32, *reinterpret_cast<float(*)[32]>(&w64[32]));
+#endif
+                    const float(&wa)[32] = *reinterpret_cast<const float(*)[32]>(&w64[0]);
+                    const float(&wb)[32] = *reinterpret_cast<const float(*)[32]>(&w64[32]);
                     tmem_wait_ld();
                     tc_fence_before();
                     __syncwarp();

@@ -72,30 +72,201 @@ __device__ __forceinline__ uint32_t warp_incl_scan(uint32_t x, int lane) {
     return x;
 }
 
+// Radix select of the K-th largest key among keys[0, n_pad) (n_pad a multiple
+// of 256; key 0 = not a candidate).  Returns the threshold key in `prefix` and
+// in `remaining` how many keys equal to it are taken (lowest index first);
+// take_all when there are at most K candidates.
+// 8 consecutive keys from shared memory (i0 a multiple of 8) with 16-byte loads.
+template <typename Key>
+__device__ __forceinline__ void load8(const Key *keys, int32_t i0, uint32_t (&k)[8]) {
+    if constexpr (sizeof(Key) == 2) {
+        const uint4 w = *reinterpret_cast<const uint4 *>(keys + i0);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            k[2 * e] = ws[e] & 0xFFFFu;
+            k[2 * e + 1] = ws[e] >> 16;
+        }
+    } else {
+        const uint4 a = *reinterpret_cast<const uint4 *>(keys + i0);
+        const uint4 b = *reinterpret_cast<const uint4 *>(keys + i0 + 4);
+        k[0] = a.x; k[1] = a.y; k[2] = a.z; k[3] = a.w;
+        k[4] = b.x; k[5] = b.y; k[6] = b.z; k[7] = b.w;
+    }
+}
+
+// Shared memory of one warp: histogram, staged keys, sample, candidate keys and ids.
+template <typename Key>
+__host__ __device__ constexpr size_t warp_smem_bytes(int64_t NB) {
+    return 1024 + ((NB + 255) / 256 * 256) * sizeof(Key) +
+           ((((NB + 255) / 256 * 256) / 8 + 255) / 256 * 256) * sizeof(Key) + 512 * sizeof(Key) +
+           512 * 2;
+}
+
+template <typename Key, int PASSES>
+__device__ __forceinline__ void radix_select(const Key *keys, int32_t n_pad, int32_t K, uint32_t *hist,
+                                             int lane, uint32_t &prefix, int32_t &remaining,
+                                             bool &take_all) {
+    constexpr int KB = 8 * (int)sizeof(Key);
+    prefix = 0;
+    uint32_t pmask = 0;
+    remaining = K;
+    take_all = false;
+#pragma unroll 1
+    for (int p = 0; p < PASSES; ++p) {
+        const int shift = KB - 8 - 8 * p;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) hist[lane * 8 + i] = 0;
+        __syncwarp();
+        for (int32_t base = 0; base < n_pad; base += 256) {
+            const int32_t i0 = base + 8 * lane;
+            uint32_t kk[8];
+            load8(keys, i0, kk);
+            uint32_t run_d = 256u, run_c = 0;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const uint32_t k = kk[e];
+                const bool m = k != 0u && (k & pmask) == prefix;
+                const uint32_t d = m ? ((k >> shift) & 255u) : 256u;
+                if (d != run_d) {
+                    if (run_c) atomicAdd(&hist[run_d], run_c);
+                    run_d = d;
+                    run_c = 0;
+                }
+                run_c += m ? 1u : 0u;
+            }
+            if (run_c) atomicAdd(&hist[run_d], run_c);
+        }
+        __syncwarp();
+        uint32_t c[8];
+        uint32_t s = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {  // lane owns bins 255-8*lane-i (descending)
+            c[i] = hist[255 - 8 * lane - i];
+            s += c[i];
+        }
+        const uint32_t incl = warp_incl_scan(s, lane);
+        const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+        if (p == 0 && total <= (uint32_t)K) {
+            take_all = true;
+            __syncwarp();
+            return;
+        }
+        const uint32_t excl = incl - s;
+        const bool mine = excl < (uint32_t)remaining && (uint32_t)remaining <= incl;
+        const uint32_t owner = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
+        uint32_t digit = 0, above = 0;
+        if (mine) {
+            uint32_t run = excl;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                if (run + c[i] >= (uint32_t)remaining) {
+                    digit = 255u - 8u * lane - i;
+                    above = run;
+                    break;
+                }
+                run += c[i];
+            }
+        }
+        digit = __shfl_sync(0xffffffffu, digit, owner);
+        above = __shfl_sync(0xffffffffu, above, owner);
+        remaining -= (int32_t)above;
+        prefix |= digit << shift;
+        pmask |= 255u << shift;
+        __syncwarp();
+    }
+}
+
+// Write the selected entries of keys[0, n) in index order to orow[0, K), then
+// -1 padding.  idx(i) maps a key slot to its block index.
+template <typename Key, typename IdxFn>
+__device__ __forceinline__ void emit_selected(const Key *keys, int32_t n, int32_t K, uint32_t prefix,
+                                              int32_t remaining, bool take_all, IdxFn idx, int lane,
+                                              int32_t *orow) {
+    int32_t pos = 0, eq_seen = 0;
+    for (int32_t base = 0; base < n && pos < K; base += 256) {
+        const int32_t i0 = base + 8 * lane;
+        uint32_t kk[8];
+        load8(keys, i0, kk);
+        uint32_t gt = 0, eq = 0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const uint32_t k = kk[e];
+            if (take_all) {
+                gt |= (k != 0u ? 1u : 0u) << e;
+            } else {
+                gt |= (k > prefix ? 1u : 0u) << e;
+                eq |= (k == prefix ? 1u : 0u) << e;
+            }
+        }
+        const uint32_t ne = (uint32_t)__popc(eq);
+        const uint32_t eincl = warp_incl_scan(ne, lane);
+        int32_t eq_budget = remaining - eq_seen - (int32_t)(eincl - ne);
+        uint32_t sel = gt;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            if ((eq >> e) & 1u) {
+                if (eq_budget > 0) sel |= 1u << e;
+                --eq_budget;
+            }
+        }
+        const uint32_t nsel = (uint32_t)__popc(sel);
+        const uint32_t si = warp_incl_scan(nsel, lane);
+        int32_t slot = pos + (int32_t)(si - nsel);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            if ((sel >> e) & 1u) {
+                if (slot < K) orow[slot] = idx(i0 + e);
+                ++slot;
+            }
+        }
+        pos += (int32_t)__shfl_sync(0xffffffffu, si, 31);
+        eq_seen += (int32_t)__shfl_sync(0xffffffffu, eincl, 31);
+    }
+    for (int32_t s2 = (pos < K ? pos : K) + lane; s2 < K; s2 += 32) orow[s2] = -1;
+}
+
+constexpr int kCandCap = 512;  // candidate buffer per warp (sampled-threshold path)
+
 template <typename T>
 __global__ void __launch_bounds__(kWarps * 32)
 topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_stride, int32_t K,
             bool vec_ok, int32_t *__restrict__ out) {
     using Key = typename KeyOf<T>::K;
     constexpr int PASSES = KeyOf<T>::kPasses;
-    constexpr int KB = 8 * (int)sizeof(Key);       // key bits
     constexpr int VT = 16 / (int)sizeof(T);        // scores per 16-byte load
     extern __shared__ __align__(16) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int32_t NBp = (NB + 255) & ~255;         // padded to whole steps (8 keys x 32 lanes)
-    uint32_t *hist = reinterpret_cast<uint32_t *>(smem) + warp * 256;
-    Key *keys = reinterpret_cast<Key *>(smem + kWarps * 256 * 4) + (size_t)warp * NBp;
+    const int32_t NS = ((NBp / 8) + 255) & ~255;   // sample slots (1 in 8), padded
+    uint8_t *wbase = smem + (size_t)warp * warp_smem_bytes<Key>(NB);
+    uint32_t *hist = reinterpret_cast<uint32_t *>(wbase);
+    Key *keys = reinterpret_cast<Key *>(wbase + 1024);
+    Key *samp = keys + NBp;
+    Key *ckey = samp + NS;
+    uint16_t *cidx = reinterpret_cast<uint16_t *>(ckey + kCandCap);
+    // the sampled threshold pays off when the row is much longer than K
+    const bool sampled = NB >= 8 * K && NB >= 512;
+    const int32_t srank = (3 * K * NS / NBp + 1) / 2 + 1;  // ~1.5x the expected sample rank of the K-th key
     for (int64_t row = (int64_t)blockIdx.x * kWarps + warp; row < rows;
          row += (int64_t)gridDim.x * kWarps) {
         const T *src = scores + row * row_stride;
+        int32_t *orow = out + row * K;
         // ---- stage keys (padding keys are 0 = never selected)
         if (vec_ok) {
             for (int32_t i = lane * VT; i < NBp; i += 32 * VT) {
                 if (i + VT <= NB) {
                     const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(src + i));
                     const T *tv = reinterpret_cast<const T *>(&raw);
+                    Key kv[VT];
 #pragma unroll
-                    for (int e = 0; e < VT; ++e) keys[i + e] = KeyOf<T>::key(tv[e]);
+                    for (int e = 0; e < VT; ++e) kv[e] = KeyOf<T>::key(tv[e]);
+                    if constexpr (sizeof(Key) * VT == 16) {
+                        *reinterpret_cast<uint4 *>(keys + i) = *reinterpret_cast<const uint4 *>(kv);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < VT; ++e) keys[i + e] = kv[e];
+                    }
                 } else {
 #pragma unroll
                     for (int e = 0; e < VT; ++e) keys[i + e] = (i + e < NB) ? KeyOf<T>::key(src[i + e]) : Key(0);
@@ -105,112 +276,61 @@ topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_
             for (int32_t i = lane; i < NBp; i += 32) keys[i] = i < NB ? KeyOf<T>::key(src[i]) : Key(0);
         }
         __syncwarp();
-        // ---- radix select of the K-th largest key
-        uint32_t prefix = 0, pmask = 0;
-        int32_t remaining = K;
-        bool take_all = false;
-#pragma unroll 1
-        for (int p = 0; p < PASSES; ++p) {
-            const int shift = KB - 8 - 8 * p;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) hist[lane * 8 + i] = 0;
+        bool done = false;
+        if (sampled) {
+            for (int32_t i = lane; i < NS; i += 32) samp[i] = (8 * i < NBp) ? keys[8 * i] : Key(0);
             __syncwarp();
+            uint32_t t0;
+            int32_t rem0;
+            bool all0;
+            radix_select<Key, PASSES>(samp, NS, srank, hist, lane, t0, rem0, all0);
+            if (all0) t0 = 1u;  // fewer sampled candidates than srank: take every candidate
+            // one pass: compact keys >= t0 (index order) into the candidate buffer
+            int32_t n = 0;
             for (int32_t base = 0; base < NBp; base += 256) {
                 const int32_t i0 = base + 8 * lane;
-                uint32_t run_d = 256u, run_c = 0;
+                uint32_t kk[8];
+                load8(keys, i0, kk);
+                uint32_t sel = 0;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) sel |= (kk[e] != 0u && kk[e] >= t0 ? 1u : 0u) << e;
+                const uint32_t ns = (uint32_t)__popc(sel);
+                const uint32_t si = warp_incl_scan(ns, lane);
+                int32_t slot = n + (int32_t)(si - ns);
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    const uint32_t k = keys[i0 + e];
-                    const bool m = k != 0u && (k & pmask) == prefix;
-                    const uint32_t d = m ? ((k >> shift) & 255u) : 256u;
-                    if (d != run_d) {
-                        if (run_c) atomicAdd(&hist[run_d], run_c);
-                        run_d = d;
-                        run_c = 0;
+                    if ((sel >> e) & 1u) {
+                        if (slot < kCandCap) {
+                            ckey[slot] = (Key)kk[e];
+                            cidx[slot] = (uint16_t)(i0 + e);
+                        }
+                        ++slot;
                     }
-                    run_c += m ? 1u : 0u;
                 }
-                if (run_c) atomicAdd(&hist[run_d], run_c);
+                n += (int32_t)__shfl_sync(0xffffffffu, si, 31);
+            }
+            if ((n >= K || all0) && n <= kCandCap) {
+                const int32_t npad = (n + 255) & ~255;
+                for (int32_t i = n + lane; i < npad; i += 32) ckey[i] = Key(0);
+                __syncwarp();
+                uint32_t prefix;
+                int32_t remaining;
+                bool take_all;
+                radix_select<Key, PASSES>(ckey, npad, K, hist, lane, prefix, remaining, take_all);
+                emit_selected(ckey, npad, K, prefix, remaining, take_all,
+                              [&](int32_t i) { return (int32_t)cidx[i]; }, lane, orow);
+                done = true;
             }
             __syncwarp();
-            uint32_t c[8];
-            uint32_t s = 0;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {  // lane owns bins 255-8*lane-i (descending)
-                c[i] = hist[255 - 8 * lane - i];
-                s += c[i];
-            }
-            const uint32_t incl = warp_incl_scan(s, lane);
-            const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
-            if (p == 0 && total <= (uint32_t)K) {
-                take_all = true;
-                break;
-            }
-            const uint32_t excl = incl - s;
-            const bool mine = excl < (uint32_t)remaining && (uint32_t)remaining <= incl;
-            const uint32_t owner = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
-            uint32_t digit = 0, above = 0;
-            if (mine) {
-                uint32_t run = excl;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    if (run + c[i] >= (uint32_t)remaining) {
-                        digit = 255u - 8u * lane - i;
-                        above = run;
-                        break;
-                    }
-                    run += c[i];
-                }
-            }
-            digit = __shfl_sync(0xffffffffu, digit, owner);
-            above = __shfl_sync(0xffffffffu, above, owner);
-            remaining -= (int32_t)above;
-            prefix |= digit << shift;
-            pmask |= 255u << shift;
-            __syncwarp();
         }
-        // ---- emit winners in index order: lane takes keys [base + 8*lane, +8)
-        int32_t *orow = out + row * K;
-        int32_t pos = 0, eq_seen = 0;
-        for (int32_t base = 0; base < NB && pos < K; base += 256) {
-            const int32_t i0 = base + 8 * lane;
-            uint32_t gt = 0, eq = 0;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const uint32_t k = keys[i0 + e];
-                if (take_all) {
-                    gt |= (k != 0u ? 1u : 0u) << e;
-                } else {
-                    gt |= (k > prefix ? 1u : 0u) << e;
-                    eq |= (k == prefix ? 1u : 0u) << e;
-                }
-            }
-            const uint32_t ne = (uint32_t)__popc(eq);
-            const uint32_t eincl = warp_incl_scan(ne, lane);
-            // ties taken: the first `remaining - eq_seen` ties of this row, in index order
-            int32_t eq_budget = remaining - eq_seen - (int32_t)(eincl - ne);
-            uint32_t sel = gt;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                if ((eq >> e) & 1u) {
-                    if (eq_budget > 0) sel |= 1u << e;
-                    --eq_budget;
-                }
-            }
-            const uint32_t nsel = (uint32_t)__popc(sel);
-            const uint32_t si = warp_incl_scan(nsel, lane);
-            int32_t slot = pos + (int32_t)(si - nsel);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                if ((sel >> e) & 1u) {
-                    if (slot < K) orow[slot] = i0 + e;
-                    ++slot;
-                }
-            }
-            pos += (int32_t)__shfl_sync(0xffffffffu, si, 31);
-            eq_seen += (int32_t)__shfl_sync(0xffffffffu, eincl, 31);
+        if (!done) {
+            uint32_t prefix;
+            int32_t remaining;
+            bool take_all;
+            radix_select<Key, PASSES>(keys, NBp, K, hist, lane, prefix, remaining, take_all);
+            emit_selected(keys, NB, K, prefix, remaining, take_all, [](int32_t i) { return i; }, lane,
+                          orow);
         }
-        for (int32_t s2 = (pos < K ? pos : K) + lane; s2 < K; s2 += 32) orow[s2] = -1;
         __syncwarp();
     }
 }
@@ -219,8 +339,7 @@ template <typename T>
 int launch_topk(const void *scores, int64_t rows, int64_t NB, int64_t row_stride, int64_t K,
                 int32_t *out, cudaStream_t s) {
     using Key = typename KeyOf<T>::K;
-    const int64_t NBp = (NB + 255) & ~(int64_t)255;
-    const size_t smem = (size_t)kWarps * (256 * 4 + NBp * sizeof(Key));
+    const size_t smem = (size_t)kWarps * warp_smem_bytes<Key>(NB);
     auto kern = topk_kernel<T>;
     UNUM_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const int64_t want = (rows + kWarps - 1) / kWarps;
