@@ -145,6 +145,26 @@ int unum_infllmv2_attn_stage1(const void *q, int64_t T, int64_t Hq, int64_t D, i
                               size_t workspace_bytes, void *stream);
 
 /*
+ * infllmv2_attn_stage1_pooled — stage 1 with the block max-pooling fused in.
+ * No single reference function: it computes, in one launch, exactly what the
+ * reference's caller gets from infllmv2_attn_stage1 followed by
+ * max_pooling_1d_varlen (max_pooling_1d_varlen.py:127-183) with block_size 64,
+ * stride 16, zero cache_lens and max_seqlen_q = 16 * out_stride (the flat row
+ * stride of the stage-1 output), so the pooling never re-reads the scores
+ * from HBM.  `out` receives the stage-1 scores as above; `pooled` bf16
+ * [Hk, T, NB] receives the block scores (+inf for the init blocks and the
+ * local window, -inf for an empty window).  Requires G >= 16.
+ */
+int unum_infllmv2_attn_stage1_pooled(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st,
+                                     int64_t q_sh, const void *k, int64_t Tk, int64_t Hk,
+                                     int64_t k_st, int64_t k_sh, const int32_t *cu_seqlens_q,
+                                     const int32_t *cu_seqlens_k, int64_t n_seq,
+                                     float softmax_scale, int causal, void *out,
+                                     int64_t out_stride, void *pooled, int64_t NB,
+                                     int64_t init_blocks, int64_t local_blocks, void *workspace,
+                                     size_t workspace_bytes, void *stream);
+
+/*
  * Status word a stage-1 launch leaves in its workspace: 0 = ok; nonzero = a
  * bounded wait inside the kernel gave up (the output is then invalid).  Reads
  * the word with a stream-ordered copy and synchronises the stream.

@@ -235,3 +235,32 @@ def test_pipeline_small_vs_oracle(dev, oracle_lib):
     np.testing.assert_array_equal(idx.cpu().numpy(), ir)
     sr = oracle_lib.get_block_table(ir, table, tb, pos, seqlen)
     np.testing.assert_array_equal(slots.cpu().numpy(), sr)
+
+
+# ---------------------------------------------------------------- fused stage 1 + pooling
+@pytest.mark.parametrize("spec", [
+    ("single_causal", [1000], None, True, 1000, 1, 2),
+    ("varlen_partial_tiles", [37, 512, 300, 1], None, True, 700, 1, 2),
+    ("noncausal", [130, 70], [40, 9], False, 4096, 2, 3),
+    ("ctx_shorter_than_keys", [2048], None, True, 512, 0, 0),
+    ("g32", [333, 64], None, True, 2000, 1, 32),
+], ids=lambda s: s[0])
+def test_stage1_pooled_equals_stage1_then_pool(spec, dev):
+    from unum_ops_b200.block_select import stage1_pooled
+    from unum_ops_b200.infllm_v2 import infllmv2_attn_stage1, max_pooling_1d_varlen
+
+    name, q_lens, k_lens, causal, ctx, init_b, local_b = spec
+    if k_lens is None:
+        k_lens = [max(cases.compressed_len(x), 1) for x in q_lens]
+    hq = 64 if name == "g32" else 32
+    c = cases.stage1_case(name, sum(map(ord, name)), q_lens, k_lens, hq, 2, causal)
+    q, k = _t(c["q"], dev, torch.bfloat16), _t(c["k"], dev, torch.bfloat16)
+    cq, ck = _t(c["cu_q"], dev), _t(c["cu_k"], dev)
+    s_f, p_f = stage1_pooled(q, k, cq, ck, max(k_lens), ctx, local_b, init_b, causal=causal)
+    s_r = infllmv2_attn_stage1(q, k, k, cq, ck, max_seqlen_k=max(k_lens), causal=causal)
+    W = s_r.shape[-1]
+    p_r = max_pooling_1d_varlen(s_r, cq, ck, torch.zeros(len(q_lens), dtype=torch.int32, device=dev),
+                                16 * W, ctx, local_b, init_b)
+    torch.cuda.synchronize()
+    assert torch.equal(s_f, s_r)
+    np.testing.assert_array_equal(p_f.float().cpu().numpy(), p_r.float().cpu().numpy())

@@ -96,6 +96,10 @@ struct Params {
     int32_t Hk;
     int32_t causal;
     float c;  // softmax_scale * log2(e)
+    // optional fused max-pooling of the scores into 64-token blocks (G >= 16):
+    // pooled[g][t][j] = max_pooling_1d_varlen(scores, max_seqlen_q = 16*W, cache 0)
+    __nv_bfloat16 *pooled;  // [Hk, T, NB] or null
+    int32_t NB, init_blocks, local_blocks;
 };
 
 struct Item {
@@ -458,6 +462,7 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                 const int tq0 = col0 / G;
                 const ulonglong2 *st4 = reinterpret_cast<const ulonglong2 *>(stats + col0);  // -b, 4 at a time
                 const uint32_t tcol2 = lane_base + col0;
+                float halo = -INFINITY;  // previous tile's last key, for fused pooling
                 for (int32_t kt = 0; kt < it.nkt; ++kt, ++sc) {
                     const uint32_t buf = sc & 1;
                     const int32_t j = kt * kBN + wq * 32 + lane;
@@ -481,8 +486,8 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                     for (int qi = 0; qi < NQ; ++qi) acc[qi][0] = acc[qi][1] = 0ull;
                     p2_chunk<G, 0>(wa, acc, st4, c2);
                     p2_chunk<G, 1>(wb, acc, st4, c2);
-                    if (kTmaStore && tq0 + NQ <= it.nq) {
-                        // stage the warpgroup's [NQ tokens x 128 keys] tile, then one TMA store
+                    if (kTmaStore) {
+                        // stage the warpgroup's [NQ tokens x 128 keys] tile in shared memory
                         const uint32_t buf_s = stc & 1;
                         __nv_bfloat16 *stg = reinterpret_cast<__nv_bfloat16 *>(
                             sgen + kOffStage + (wg * 2 + buf_s) * kStageWg);
@@ -498,10 +503,63 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                         fence_async_shared();
                         if (wq == 0 && lane == 0) bulk_wait_read_all();  // previous store left its buffer
                         named_bar_sync(2 + wg, 128);
-                        if (wq == 0 && lane == 0) {
-                            tma_store_2d(&tmO, smem_u32(stg), kt * kBN,
-                                         (int32_t)((int64_t)it.g * p.T + it.t0 + tq0));
-                            bulk_commit();
+                        const int t_idx = wq * 32 + lane;
+                        if (tq0 + NQ <= it.nq) {  // whole tile belongs to this sequence: one TMA store
+                            if (t_idx == 0) {
+                                tma_store_2d(&tmO, smem_u32(stg), kt * kBN,
+                                             (int32_t)((int64_t)it.g * p.T + it.t0 + tq0));
+                                bulk_commit();
+                            }
+                        } else {  // sequence ends inside the tile: copy its rows only
+                            for (int e = t_idx; e < NQ * kBN; e += 128) {
+                                const int tq = tq0 + e / kBN;
+                                const int64_t col = (int64_t)kt * kBN + (e % kBN);
+                                if (tq < it.nq && col < p.out_stride)
+                                    out_g[(it.t0 + tq) * p.out_stride + col] = stg[e];
+                            }
+                        }
+                        if (p.pooled) {
+                            // warp wq pools token tq0+wq: lane = block in this tile, its window is
+                            // keys [4*lane-1, 4*lane+3]; key 4*lane-1 is the previous lane's last
+                            // key (shuffle) or, for lane 0, the previous tile's last key (halo)
+                            for (int qi = wq; qi < NQ; qi += 4) {
+                                const int tq = tq0 + qi;
+                                const uint2 raw = *reinterpret_cast<const uint2 *>(stg + qi * kBN + 4 * lane);
+                                const __nv_bfloat162 lo2 = *reinterpret_cast<const __nv_bfloat162 *>(&raw.x);
+                                const __nv_bfloat162 hi2 = *reinterpret_cast<const __nv_bfloat162 *>(&raw.y);
+                                float x[4] = {__low2float(lo2), __high2float(lo2), __low2float(hi2), __high2float(hi2)};
+                                float left = __shfl_up_sync(0xffffffffu, x[3], 1);
+                                if (lane == 0) left = halo;
+                                halo = __shfl_sync(0xffffffffu, x[3], 31);
+                                const int32_t c0k = kt * kBN + 4 * lane;  // global key of x[0]
+                                if (c0k + 3 >= it.k_len || c0k == 0) {
+#pragma unroll
+                                    for (int i = 0; i < 4; ++i)
+                                        if (c0k + i >= it.k_len) x[i] = -INFINITY;
+                                    if (c0k - 1 < 0 || c0k - 1 >= it.k_len) left = -INFINITY;
+                                }
+                                const float mx = fmaxf(fmax3(left, x[0], x[1]), fmaxf(x[2], x[3]));
+                                if (tq < it.nq) {
+                                    const int32_t jg = kt * 32 + lane;
+                                    const int32_t off_bq = (it.local0 + tq) / 64;
+                                    __nv_bfloat16 *prow = p.pooled + ((int64_t)it.g * p.T + it.t0 + tq) * p.NB;
+                                    if (jg < p.NB) {
+                                        const bool minf = jg < p.init_blocks || (off_bq >= jg && off_bq <= jg + p.local_blocks);
+                                        const bool has = 4 * jg - 1 < it.k_len;
+                                        prow[jg] = __float2bfloat16_rn(minf ? INFINITY : (has ? mx : -INFINITY));
+                                    }
+                                    if (lane == 31 && kt + 1 == it.nkt && jg + 1 < p.NB) {
+                                        // first block past the computed tiles: key 128*nkt-1 plus zeros
+                                        const int32_t jn = jg + 1, cl = kt * kBN + kBN - 1;
+                                        float m2 = -INFINITY;
+                                        if (cl < it.k_len) m2 = x[3];
+                                        if (cl + 1 < it.k_len) m2 = fmaxf(m2, 0.f);
+                                        const bool minf = jn < p.init_blocks || (off_bq >= jn && off_bq <= jn + p.local_blocks);
+                                        const bool has = 4 * jn - 1 < it.k_len;
+                                        prow[jn] = __float2bfloat16_rn(minf ? INFINITY : (has ? m2 : -INFINITY));
+                                    }
+                                }
+                            }
                         }
                         ++stc;
                     } else if (j < p.out_stride) {
@@ -534,6 +592,22 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                         *dst = z;
                     }
                 }
+                if (p.pooled) {
+                    // blocks whose windows hold only keys past the computed tiles: zeros while
+                    // inside k_len, else an empty window (-inf); +inf where init/local masks
+                    const int32_t jstart = it.nkt > 0 ? it.nkt * 32 + 1 : 0;
+                    const int32_t nj = p.NB - jstart;
+                    if (nj > 0) {
+                        for (int64_t e = tid; e < (int64_t)nj * it.nq; e += kEpiWarps * 32) {
+                            const int32_t tq = (int32_t)(e / nj), jg = jstart + (int32_t)(e - (int64_t)tq * nj);
+                            const int32_t off_bq = (it.local0 + tq) / 64;
+                            const bool minf = jg < p.init_blocks || (off_bq >= jg && off_bq <= jg + p.local_blocks);
+                            const bool has = 4 * jg - 1 < it.k_len;
+                            p.pooled[((int64_t)it.g * p.T + it.t0 + tq) * p.NB + jg] =
+                                __float2bfloat16_rn(minf ? INFINITY : (has ? 0.f : -INFINITY));
+                        }
+                    }
+                }
             }
         }
         if (wq == 0 && lane == 0) bulk_wait_all();  // output stores complete before exit
@@ -558,7 +632,8 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
 // [cu_q[0], cu_q[n_seq]) keep the reference's torch.zeros value).
 __global__ void __launch_bounds__(1024)
 stage1_prologue(const int32_t *__restrict__ cu_q, int32_t n_seq, int32_t QT, int32_t *ws,
-                __nv_bfloat16 *out, int64_t T, int32_t Hk, int64_t out_stride) {
+                __nv_bfloat16 *out, int64_t T, int32_t Hk, int64_t out_stride,
+                __nv_bfloat16 *pooled, int32_t NB, int32_t init_blocks, int32_t local_blocks) {
     __shared__ int32_t warp_sums[32];
     __shared__ int32_t carry_s;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -612,6 +687,13 @@ stage1_prologue(const int32_t *__restrict__ cu_q, int32_t n_seq, int32_t QT, int
             }
             uint4 *row = reinterpret_cast<uint4 *>(out + ((int64_t)g * T + t) * out_stride);
             for (int64_t e = tid; e < per_row; e += 1024) row[e] = make_uint4(0, 0, 0, 0);
+            if (pooled) {  // no sequence: k_len 0, local block 0 (max_pooling_1d_varlen.py:69-80)
+                __nv_bfloat16 *prow = pooled + ((int64_t)g * T + t) * NB;
+                for (int32_t j = tid; j < NB; j += 1024) {
+                    const bool minf = j < init_blocks || (0 >= j && 0 <= j + local_blocks);
+                    prow[j] = __float2bfloat16_rn(minf ? INFINITY : -INFINITY);
+                }
+            }
         }
     }
 }
@@ -672,14 +754,14 @@ extern "C" size_t unum_stage1_workspace_size(int64_t n_seq) {
     return (size_t)(((kWsTiles + n_seq + 1) * 4 + 15) / 16 * 16);
 }
 
-extern "C" int unum_infllmv2_attn_stage1(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st,
-                                         int64_t q_sh, const void *k, int64_t Tk, int64_t Hk,
-                                         int64_t k_st, int64_t k_sh, const int32_t *cu_seqlens_q,
-                                         const int32_t *cu_seqlens_k, int64_t n_seq,
-                                         float softmax_scale, int causal, void *out,
-                                         int64_t out_stride, void *workspace,
-                                         size_t workspace_bytes, void *stream) {
-    unum::clear_error();
+namespace {
+
+int stage1_run(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, int64_t q_sh,
+               const void *k, int64_t Tk, int64_t Hk, int64_t k_st, int64_t k_sh,
+               const int32_t *cu_seqlens_q, const int32_t *cu_seqlens_k, int64_t n_seq,
+               float softmax_scale, int causal, void *out, int64_t out_stride, void *workspace,
+               size_t workspace_bytes, void *stream, void *pooled, int64_t NB, int64_t init_blocks,
+               int64_t local_blocks) {
     UNUM_CHECK_ARG(T >= 0 && Tk >= 0 && Hq > 0 && Hk > 0 && n_seq >= 0 && out_stride >= 0,
                    "bad sizes");
     UNUM_CHECK_ARG(Hq % Hk == 0, "n_heads (%lld) must be a multiple of n_kv_heads (%lld)",
@@ -706,9 +788,15 @@ extern "C" int unum_infllmv2_attn_stage1(const void *q, int64_t T, int64_t Hq, i
     int32_t *ws = (int32_t *)workspace;
     const int QT = (int)(kRows / G);
     stage1_prologue<<<1, 1024, 0, s>>>(cu_seqlens_q, (int32_t)n_seq, QT, ws,
-                                       (__nv_bfloat16 *)out, T, (int32_t)Hk, out_stride);
+                                       (__nv_bfloat16 *)out, T, (int32_t)Hk, out_stride,
+                                       (__nv_bfloat16 *)pooled, (int32_t)NB, (int32_t)init_blocks,
+                                       (int32_t)local_blocks);
     if (int rc = unum::check_launch("stage1_prologue")) return rc;
     if (n_seq == 0) return UNUM_OK;
+    if (Tk == 0 && pooled) {
+        unum::set_error("fused pooling needs at least one compressed key");
+        return UNUM_ERR_UNSUPPORTED;
+    }
     if (Tk == 0) {  // no compressed keys anywhere: every row is zero
         UNUM_CHECK_CUDA(cudaMemsetAsync(out, 0, (size_t)Hk * T * out_stride * 2, s));
         return UNUM_OK;
@@ -750,6 +838,10 @@ extern "C" int unum_infllmv2_attn_stage1(const void *q, int64_t T, int64_t Hq, i
     p.Hk = (int32_t)Hk;
     p.causal = causal ? 1 : 0;
     p.c = softmax_scale * kLog2e;
+    p.pooled = (__nv_bfloat16 *)pooled;
+    p.NB = (int32_t)NB;
+    p.init_blocks = (int32_t)init_blocks;
+    p.local_blocks = (int32_t)local_blocks;
     switch (G) {
         case 2: return launch_main<2>(mq, mk, mo, p, T, s);
         case 4: return launch_main<4>(mq, mk, mo, p, T, s);
@@ -757,6 +849,42 @@ extern "C" int unum_infllmv2_attn_stage1(const void *q, int64_t T, int64_t Hq, i
         case 16: return launch_main<16>(mq, mk, mo, p, T, s);
         default: return launch_main<32>(mq, mk, mo, p, T, s);
     }
+}
+
+}  // namespace
+
+extern "C" int unum_infllmv2_attn_stage1(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st,
+                                         int64_t q_sh, const void *k, int64_t Tk, int64_t Hk,
+                                         int64_t k_st, int64_t k_sh, const int32_t *cu_seqlens_q,
+                                         const int32_t *cu_seqlens_k, int64_t n_seq,
+                                         float softmax_scale, int causal, void *out,
+                                         int64_t out_stride, void *workspace,
+                                         size_t workspace_bytes, void *stream) {
+    unum::clear_error();
+    return stage1_run(q, T, Hq, D, q_st, q_sh, k, Tk, Hk, k_st, k_sh, cu_seqlens_q, cu_seqlens_k,
+                      n_seq, softmax_scale, causal, out, out_stride, workspace, workspace_bytes,
+                      stream, nullptr, 0, 0, 0);
+}
+
+extern "C" int unum_infllmv2_attn_stage1_pooled(
+    const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, int64_t q_sh, const void *k,
+    int64_t Tk, int64_t Hk, int64_t k_st, int64_t k_sh, const int32_t *cu_seqlens_q,
+    const int32_t *cu_seqlens_k, int64_t n_seq, float softmax_scale, int causal, void *out,
+    int64_t out_stride, void *pooled, int64_t NB, int64_t init_blocks, int64_t local_blocks,
+    void *workspace, size_t workspace_bytes, void *stream) {
+    unum::clear_error();
+    UNUM_CHECK_ARG(pooled != nullptr && NB > 0, "pooled output required");
+    UNUM_CHECK_ARG(NB < (int64_t)1 << 30 && init_blocks >= -(1 << 30) && init_blocks < (1 << 30) &&
+                       local_blocks >= -(1 << 30) && local_blocks < (1 << 30),
+                   "pooling parameters out of range");
+    if (Hk <= 0 || Hq % Hk != 0 || Hq / Hk < 16) {
+        unum::set_error("fused pooling needs a head group of at least 16 (got %lld/%lld)",
+                        (long long)Hq, (long long)Hk);
+        return UNUM_ERR_UNSUPPORTED;
+    }
+    return stage1_run(q, T, Hq, D, q_st, q_sh, k, Tk, Hk, k_st, k_sh, cu_seqlens_q, cu_seqlens_k,
+                      n_seq, softmax_scale, causal, out, out_stride, workspace, workspace_bytes,
+                      stream, pooled, NB, init_blocks, local_blocks);
 }
 
 extern "C" int unum_stage1_status(const void *workspace, void *stream, int32_t *status_out) {
