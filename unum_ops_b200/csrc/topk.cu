@@ -8,18 +8,18 @@
 // the one the reference's block-table tests feed to get_block_table
 // (test/test_sparse_kernel.py:80-87).
 //
-// B200 design: one warp per row.  The row is staged once in shared memory as
-// order-preserving keys — 16-bit for bf16/fp16 scores, 32-bit for fp32 —
-// with excluded entries mapped to key 0; 16-byte vector loads from HBM when
-// the rows are aligned.  A radix select (8-bit digits, a 256-bin warp-private
-// histogram, a warp scan to find the digit holding the K-th key) yields the
-// threshold key in 2 passes (16-bit) or 4 (fp32).  Each lane walks 8
-// consecutive keys per step and adds a run of equal digits with one
-// shared-memory atomic, so long runs of equal scores (the zero-score blocks
-// past a causal query) cost one atomic per 8 keys.  The emit sweep walks the
-// row in index order, 8 keys per lane per step, with warp scans for the tie
-// count and the output slot, so winners come out sorted and only the
-// lowest-index ties are taken.
+// B200 design: one warp per row at a time; each warp owns a run of
+// consecutive rows.  The row is loaded once (16-byte vectors when aligned),
+// turned into order-preserving keys — 16-bit for bf16/fp16 scores, 32-bit for
+// fp32, excluded entries = key 0 — and staged in shared memory.  The same pass
+// compacts the keys at or above the previous row's threshold minus a margin
+// into a small candidate buffer (neighbouring rows of pooled scores are nearly
+// identical); the exact selection — a radix select with 8-bit digits (2 passes
+// for 16-bit keys, 4 for fp32), run-length aggregated shared-memory histogram
+// atomics and warp scans — then runs on the candidates only, or on the whole
+// staged row when the bound missed.  The emit sweep walks keys in index order
+// with warp scans, so winners come out sorted and only the lowest-index ties
+// are taken.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -95,12 +95,10 @@ __device__ __forceinline__ void load8(const Key *keys, int32_t i0, uint32_t (&k)
     }
 }
 
-// Shared memory of one warp: histogram, staged keys, sample, candidate keys and ids.
+// Shared memory of one warp: histogram, staged keys, candidate keys and ids.
 template <typename Key>
 __host__ __device__ constexpr size_t warp_smem_bytes(int64_t NB) {
-    return 1024 + ((NB + 255) / 256 * 256) * sizeof(Key) +
-           ((((NB + 255) / 256 * 256) / 8 + 255) / 256 * 256) * sizeof(Key) + 512 * sizeof(Key) +
-           512 * 2;
+    return 1024 + ((NB + 255) / 256 * 256) * sizeof(Key) + 512 * sizeof(Key) + 512 * 2;
 }
 
 template <typename Key, int PASSES>
@@ -226,111 +224,115 @@ __device__ __forceinline__ void emit_selected(const Key *keys, int32_t n, int32_
     for (int32_t s2 = (pos < K ? pos : K) + lane; s2 < K; s2 += 32) orow[s2] = -1;
 }
 
-constexpr int kCandCap = 512;  // candidate buffer per warp (sampled-threshold path)
+constexpr int kCandCap = 512;   // candidate buffer per warp
+// threshold margin in key steps: 32 bf16/fp16 steps (bf16: 2^(32/128) = 19 % in value);
+// the same relative width for 32-bit keys
+template <typename Key> constexpr uint32_t kMargin = sizeof(Key) == 2 ? 32u : (32u << 16);
 
+// 8 consecutive scores of a row as keys (vector loads when aligned).
+template <typename T>
+__device__ __forceinline__ void load8_keys(const T *src, int32_t i0, int32_t NB, bool vec_ok,
+                                           uint32_t (&k)[8]) {
+    constexpr int VT = 16 / (int)sizeof(T);
+    if (vec_ok && i0 + 8 <= NB) {
+#pragma unroll
+        for (int h = 0; h < 8 / VT; ++h) {
+            const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(src + i0 + h * VT));
+            const T *tv = reinterpret_cast<const T *>(&raw);
+#pragma unroll
+            for (int e = 0; e < VT; ++e) k[h * VT + e] = KeyOf<T>::key(tv[e]);
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) k[e] = (i0 + e < NB) ? KeyOf<T>::key(src[i0 + e]) : 0u;
+    }
+}
+
+// Each warp owns a contiguous run of rows.  Neighbouring rows of pooled block
+// scores are nearly identical, so the previous row's threshold key, lowered by
+// kMargin, is a good lower bound for this row's: the pass that loads the row
+// also compacts the keys at or above it (in index order) into a candidate
+// buffer, and the exact selection runs on those candidates only.  When the
+// bound misses (fewer than K candidates, or more than the buffer holds) the
+// full radix select runs on the staged row instead.  Results never depend on
+// which path ran.
 template <typename T>
 __global__ void __launch_bounds__(kWarps * 32)
 topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_stride, int32_t K,
-            bool vec_ok, int32_t *__restrict__ out) {
+            bool vec_ok, int64_t rows_per_warp, int32_t *__restrict__ out) {
     using Key = typename KeyOf<T>::K;
     constexpr int PASSES = KeyOf<T>::kPasses;
-    constexpr int VT = 16 / (int)sizeof(T);        // scores per 16-byte load
     extern __shared__ __align__(16) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int32_t NBp = (NB + 255) & ~255;         // padded to whole steps (8 keys x 32 lanes)
-    const int32_t NS = ((NBp / 8) + 255) & ~255;   // sample slots (1 in 8), padded
+    const int32_t NBp = (NB + 255) & ~255;  // padded to whole steps (8 keys x 32 lanes)
     uint8_t *wbase = smem + (size_t)warp * warp_smem_bytes<Key>(NB);
     uint32_t *hist = reinterpret_cast<uint32_t *>(wbase);
     Key *keys = reinterpret_cast<Key *>(wbase + 1024);
-    Key *samp = keys + NBp;
-    Key *ckey = samp + NS;
+    Key *ckey = keys + NBp;
     uint16_t *cidx = reinterpret_cast<uint16_t *>(ckey + kCandCap);
-    // the sampled threshold pays off when the row is much longer than K
-    const bool sampled = NB >= 8 * K && NB >= 512;
-    const int32_t srank = (3 * K * NS / NBp + 1) / 2 + 1;  // ~1.5x the expected sample rank of the K-th key
-    for (int64_t row = (int64_t)blockIdx.x * kWarps + warp; row < rows;
-         row += (int64_t)gridDim.x * kWarps) {
+    const int64_t gw = (int64_t)blockIdx.x * kWarps + warp;
+    const int64_t r0 = gw * rows_per_warp;
+    const int64_t r1 = r0 + rows_per_warp < rows ? r0 + rows_per_warp : rows;
+    uint32_t tau_prev = 0;  // threshold key of the previous row (0: none)
+    for (int64_t row = r0; row < r1; ++row) {
         const T *src = scores + row * row_stride;
         int32_t *orow = out + row * K;
-        // ---- stage keys (padding keys are 0 = never selected)
-        if (vec_ok) {
-            for (int32_t i = lane * VT; i < NBp; i += 32 * VT) {
-                if (i + VT <= NB) {
-                    const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(src + i));
-                    const T *tv = reinterpret_cast<const T *>(&raw);
-                    Key kv[VT];
-#pragma unroll
-                    for (int e = 0; e < VT; ++e) kv[e] = KeyOf<T>::key(tv[e]);
-                    if constexpr (sizeof(Key) * VT == 16) {
-                        *reinterpret_cast<uint4 *>(keys + i) = *reinterpret_cast<const uint4 *>(kv);
-                    } else {
-#pragma unroll
-                        for (int e = 0; e < VT; ++e) keys[i + e] = kv[e];
-                    }
-                } else {
-#pragma unroll
-                    for (int e = 0; e < VT; ++e) keys[i + e] = (i + e < NB) ? KeyOf<T>::key(src[i + e]) : Key(0);
-                }
+        const uint32_t t0 = tau_prev > kMargin<Key> ? tau_prev - kMargin<Key> : (tau_prev ? 1u : 0u);
+        int32_t n = 0;
+        for (int32_t base = 0; base < NBp; base += 256) {
+            const int32_t i0 = base + 8 * lane;
+            uint32_t kk[8];
+            load8_keys<T>(src, i0, NB, vec_ok, kk);
+            if constexpr (sizeof(Key) == 2) {
+                uint4 w;
+                w.x = kk[0] | (kk[1] << 16);
+                w.y = kk[2] | (kk[3] << 16);
+                w.z = kk[4] | (kk[5] << 16);
+                w.w = kk[6] | (kk[7] << 16);
+                *reinterpret_cast<uint4 *>(keys + i0) = w;
+            } else {
+                *reinterpret_cast<uint4 *>(keys + i0) = make_uint4(kk[0], kk[1], kk[2], kk[3]);
+                *reinterpret_cast<uint4 *>(keys + i0 + 4) = make_uint4(kk[4], kk[5], kk[6], kk[7]);
             }
-        } else {
-            for (int32_t i = lane; i < NBp; i += 32) keys[i] = i < NB ? KeyOf<T>::key(src[i]) : Key(0);
-        }
-        __syncwarp();
-        bool done = false;
-        if (sampled) {
-            for (int32_t i = lane; i < NS; i += 32) samp[i] = (8 * i < NBp) ? keys[8 * i] : Key(0);
-            __syncwarp();
-            uint32_t t0;
-            int32_t rem0;
-            bool all0;
-            radix_select<Key, PASSES>(samp, NS, srank, hist, lane, t0, rem0, all0);
-            if (all0) t0 = 1u;  // fewer sampled candidates than srank: take every candidate
-            // one pass: compact keys >= t0 (index order) into the candidate buffer
-            int32_t n = 0;
-            for (int32_t base = 0; base < NBp; base += 256) {
-                const int32_t i0 = base + 8 * lane;
-                uint32_t kk[8];
-                load8(keys, i0, kk);
+            if (t0) {
                 uint32_t sel = 0;
 #pragma unroll
-                for (int e = 0; e < 8; ++e) sel |= (kk[e] != 0u && kk[e] >= t0 ? 1u : 0u) << e;
+                for (int e = 0; e < 8; ++e) sel |= (kk[e] >= t0 ? 1u : 0u) << e;  // t0 >= 1: excludes key 0
                 const uint32_t ns = (uint32_t)__popc(sel);
                 const uint32_t si = warp_incl_scan(ns, lane);
                 int32_t slot = n + (int32_t)(si - ns);
+                if (sel) {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    if ((sel >> e) & 1u) {
-                        if (slot < kCandCap) {
-                            ckey[slot] = (Key)kk[e];
-                            cidx[slot] = (uint16_t)(i0 + e);
+                    for (int e = 0; e < 8; ++e) {
+                        if ((sel >> e) & 1u) {
+                            if (slot < kCandCap) {
+                                ckey[slot] = (Key)kk[e];
+                                cidx[slot] = (uint16_t)(i0 + e);
+                            }
+                            ++slot;
                         }
-                        ++slot;
                     }
                 }
                 n += (int32_t)__shfl_sync(0xffffffffu, si, 31);
             }
-            if ((n >= K || all0) && n <= kCandCap) {
-                const int32_t npad = (n + 255) & ~255;
-                for (int32_t i = n + lane; i < npad; i += 32) ckey[i] = Key(0);
-                __syncwarp();
-                uint32_t prefix;
-                int32_t remaining;
-                bool take_all;
-                radix_select<Key, PASSES>(ckey, npad, K, hist, lane, prefix, remaining, take_all);
-                emit_selected(ckey, npad, K, prefix, remaining, take_all,
-                              [&](int32_t i) { return (int32_t)cidx[i]; }, lane, orow);
-                done = true;
-            }
-            __syncwarp();
         }
-        if (!done) {
-            uint32_t prefix;
-            int32_t remaining;
-            bool take_all;
+        __syncwarp();
+        uint32_t prefix;
+        int32_t remaining;
+        bool take_all;
+        if (t0 && n >= K && n <= kCandCap) {
+            const int32_t npad = (n + 255) & ~255;
+            for (int32_t i = n + lane; i < npad; i += 32) ckey[i] = Key(0);
+            __syncwarp();
+            radix_select<Key, PASSES>(ckey, npad, K, hist, lane, prefix, remaining, take_all);
+            emit_selected(ckey, npad, K, prefix, remaining, take_all,
+                          [&](int32_t i) { return (int32_t)cidx[i]; }, lane, orow);
+        } else {
             radix_select<Key, PASSES>(keys, NBp, K, hist, lane, prefix, remaining, take_all);
             emit_selected(keys, NB, K, prefix, remaining, take_all, [](int32_t i) { return i; }, lane,
                           orow);
         }
+        tau_prev = take_all ? 0u : prefix;
         __syncwarp();
     }
 }
@@ -342,12 +344,15 @@ int launch_topk(const void *scores, int64_t rows, int64_t NB, int64_t row_stride
     const size_t smem = (size_t)kWarps * warp_smem_bytes<Key>(NB);
     auto kern = topk_kernel<T>;
     UNUM_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    // a few long runs of consecutive rows per warp, so most rows reuse a threshold
     const int64_t want = (rows + kWarps - 1) / kWarps;
-    const int64_t cap = (int64_t)unum::sm_count() * 64;
+    const int64_t cap = (int64_t)unum::sm_count() * 6;  // one resident wave (~29 KB of shared memory a block)
     const int grid = (int)(want < cap ? want : cap);
+    const int64_t nwarps = (int64_t)grid * kWarps;
+    const int64_t rows_per_warp = (rows + nwarps - 1) / nwarps;
     const bool vec_ok = unum::aligned16(scores) && ((row_stride * (int64_t)sizeof(T)) % 16 == 0);
     kern<<<grid, kWarps * 32, smem, s>>>((const T *)scores, rows, (int32_t)NB, row_stride, (int32_t)K,
-                                         vec_ok, out);
+                                         vec_ok, rows_per_warp, out);
     return unum::check_launch("topk_kernel");
 }
 
