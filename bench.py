@@ -359,6 +359,79 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------------------ decode batch (config 4)
+def run_decode(args):
+    """512 sequences x 1 query token, contexts U[4096, 65536], every rank
+    its own batch (weak scaling).  A step is block_select on the batch."""
+    import torch
+    import torch.distributed as dist
+
+    import unum_ops_b200
+    from unum_ops_b200 import block_select
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
+        dist.init_process_group("nccl", device_id=dev)
+    unum_ops_b200.load()
+    B = 512
+    rng = np.random.default_rng(4 + rank)
+    ctx = rng.integers(4096, 65537, size=B)
+    k_lens = (ctx - 32) // 16 + 1
+    g = torch.Generator(device=dev).manual_seed(4 + rank)
+    q = torch.randn(B, HQ, D, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(int(k_lens.sum()), HK, D, generator=g, device=dev).to(torch.bfloat16)
+    cu_q = torch.arange(B + 1, dtype=torch.int32, device=dev)
+    cu_k = torch.from_numpy(np.concatenate([[0], np.cumsum(k_lens)]).astype(np.int32)).to(dev)
+    table = torch.from_numpy(rng.integers(0, 1 << 20, size=(B, 1024)).astype(np.int32)).to(dev)
+    tb = torch.arange(B, dtype=torch.int32, device=dev)
+    pos = torch.from_numpy(ctx.astype(np.int32)).to(dev)
+    cache = torch.from_numpy((ctx - 1).astype(np.int32)).to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return block_select(q, k, cu_q, cu_k, int(k_lens.max()), table, tb, pos, pos,
+                            max_context_len=65536, cache_lens=cache)
+
+    for _ in range(args.warmup):
+        step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    kbytes = int(k_lens.sum()) * HK * D * 2
+    if rank == 0:
+        hbm = load_peaks()[0]
+        print(json.dumps({
+            "metric": "decode block selection, sequences/s (512 x 1 query, contexts U[4096,65536])",
+            "value": world * B / (ms * 1e-3), "unit": "sequences/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded)", "config": {"workload": "C4 decode batch",
+                                                     "k_cmp_bytes": kbytes},
+            "k_cmp_stream_gbs": kbytes / (ms * 1e-3) / 1e9,
+            "k_cmp_stream_frac": kbytes / (ms * 1e-3) / 1e9 / hbm}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 # ------------------------------------------------------------------ CPU baseline
 def cpu_baseline(args, sample_tokens=2048, repeats=1, host=None):
     """Time the reference's semantics on the host (C port in oracle/, all threads)
@@ -448,6 +521,8 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=8192,
                     help="tokens of the CPU-baseline sample (0: skip)")
     ap.add_argument("--ref-sample", type=int, default=2048)
+    ap.add_argument("--workload", default="prefill", choices=["prefill", "decode"],
+                    help="prefill: the 128k headline (config 3); decode: config 4")
     ap.add_argument("--seqlen", type=int, default=131072,
                     help="prefill length (default: the 128k headline workload)")
     args = ap.parse_args()
@@ -458,6 +533,8 @@ def main():
     args.ref_sample = min(args.ref_sample, L_SEQ)
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "decode":
+        run_decode(args)
     else:
         run_ours(args)
 

@@ -423,7 +423,18 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                 const int colh = (wg & 1) * 64;
                 float m = -INFINITY, l = 0.f;
                 const uint32_t tcol = lane_base + (wg >> 1) * 128 + colh;
-                for (int32_t kt = 0; kt < it.nkt; ++kt, ++sc) {
+                // a warp whose rows all belong to tokens past the sequence end (decode tiles,
+                // a sequence's last tile) only keeps the buffer handshake going
+                const bool warp_idle1 = ((wg >> 1) * 128 + wq * 32) / G >= it.nq;
+                for (int32_t kt = 0; warp_idle1 && kt < it.nkt; ++kt, ++sc) {
+                    const uint32_t buf = sc & 1;
+                    wait_bar(sy, sy.s_full + 8 * buf, (sc >> 1) & 1, 6);
+                    tc_fence_after();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(sy.s_empty + 8 * buf);
+                }
+                for (int32_t kt = 0; !warp_idle1 && kt < it.nkt; ++kt, ++sc) {
                     const uint32_t buf = sc & 1;
                     wait_bar(sy, sy.s_full + 8 * buf, (sc >> 1) & 1, 6);
                     tc_fence_after();
@@ -463,7 +474,16 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                 const ulonglong2 *st4 = reinterpret_cast<const ulonglong2 *>(stats + col0);  // -b, 4 at a time
                 const uint32_t tcol2 = lane_base + col0;
                 float halo = -INFINITY;  // previous tile's last key, for fused pooling
-                for (int32_t kt = 0; kt < it.nkt; ++kt, ++sc) {
+                const bool wg_idle2 = tq0 >= it.nq;  // every token of this warpgroup is past the end
+                for (int32_t kt = 0; wg_idle2 && kt < it.nkt; ++kt, ++sc) {
+                    const uint32_t buf = sc & 1;
+                    wait_bar(sy, sy.s_full + 8 * buf, (sc >> 1) & 1, 7);
+                    tc_fence_after();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(sy.s_empty + 8 * buf);
+                }
+                for (int32_t kt = 0; !wg_idle2 && kt < it.nkt; ++kt, ++sc) {
                     const uint32_t buf = sc & 1;
                     const int32_t j = kt * kBN + wq * 32 + lane;
                     wait_bar(sy, sy.s_full + 8 * buf, (sc >> 1) & 1, 7);
