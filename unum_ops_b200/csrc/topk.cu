@@ -31,6 +31,16 @@ constexpr int kWarps = 4;
 constexpr int kMaxNB = 4096;
 constexpr int kMaxK = 1024;
 
+template <typename T> __device__ __forceinline__ float to_f(T v);
+template <> __device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f(float v);
+template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+
 // Order-preserving keys: larger score -> larger key; -inf and NaN -> 0.
 template <typename T> struct KeyOf;
 template <> struct KeyOf<float> {
@@ -201,23 +211,12 @@ __device__ __forceinline__ void emit_selected(const Key *keys, int32_t n, int32_
         const uint32_t eincl = warp_incl_scan(ne, lane);
         int32_t eq_budget = remaining - eq_seen - (int32_t)(eincl - ne);
         uint32_t sel = gt;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            if ((eq >> e) & 1u) {
-                if (eq_budget > 0) sel |= 1u << e;
-                --eq_budget;
-            }
-        }
+        for (uint32_t m = eq; m != 0u && eq_budget > 0; m &= m - 1u, --eq_budget)
+            sel |= m & (0u - m);  // lowest remaining tie, in index order
         const uint32_t nsel = (uint32_t)__popc(sel);
         const uint32_t si = warp_incl_scan(nsel, lane);
         int32_t slot = pos + (int32_t)(si - nsel);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            if ((sel >> e) & 1u) {
-                if (slot < K) orow[slot] = idx(i0 + e);
-                ++slot;
-            }
-        }
+        for (uint32_t m = sel; m != 0u && slot < K; m &= m - 1u, ++slot) orow[slot] = idx(i0 + __ffs(m) - 1);
         pos += (int32_t)__shfl_sync(0xffffffffu, si, 31);
         eq_seen += (int32_t)__shfl_sync(0xffffffffu, eincl, 31);
     }
@@ -228,6 +227,9 @@ constexpr int kCandCap = 512;   // candidate buffer per warp
 // threshold margin in key steps: 32 bf16/fp16 steps (bf16: 2^(32/128) = 19 % in value);
 // the same relative width for 32-bit keys
 template <typename Key> constexpr uint32_t kMargin = sizeof(Key) == 2 ? 32u : (32u << 16);
+// key of the most negative finite score: the candidate bound never goes below it,
+// so -inf (and NaN) scores are never counted as candidates
+template <typename Key> constexpr uint32_t kMinFinite = sizeof(Key) == 2 ? 0x80u : 0x00800000u;
 
 // 8 consecutive scores of a row as keys (vector loads when aligned).
 template <typename T>
@@ -248,14 +250,30 @@ __device__ __forceinline__ void load8_keys(const T *src, int32_t i0, int32_t NB,
     }
 }
 
+// Score value whose key is k (inverse of KeyOf<T>::key for non-excluded keys).
+template <typename T> __device__ __forceinline__ float key_value(uint32_t k);
+template <> __device__ __forceinline__ float key_value<float>(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+template <> __device__ __forceinline__ float key_value<__nv_bfloat16>(uint32_t k) {
+    const uint32_t u = (k & 0x8000u) ? (k & 0x7FFFu) : (~k & 0xFFFFu);
+    return __bfloat162float(__ushort_as_bfloat16((unsigned short)u));
+}
+template <> __device__ __forceinline__ float key_value<__half>(uint32_t k) {
+    const uint32_t u = (k & 0x8000u) ? (k & 0x7FFFu) : (~k & 0xFFFFu);
+    return __half2float(__ushort_as_half((unsigned short)u));
+}
+
 // Each warp owns a contiguous run of rows.  Neighbouring rows of pooled block
-// scores are nearly identical, so the previous row's threshold key, lowered by
-// kMargin, is a good lower bound for this row's: the pass that loads the row
-// also compacts the keys at or above it (in index order) into a candidate
-// buffer, and the exact selection runs on those candidates only.  When the
-// bound misses (fewer than K candidates, or more than the buffer holds) the
-// full radix select runs on the staged row instead.  Results never depend on
-// which path ran.
+// scores are nearly identical, so the previous row's threshold, lowered by
+// kMargin key steps, is a good lower bound for this row's.  The pass that
+// loads the row compares every score with that bound (as a float: the key
+// order is the float order, and a superset of candidates is harmless) and
+// compacts the ones at or above it, in index order, into a candidate buffer;
+// keys are computed for candidates only, and the exact selection runs on them.
+// When the bound misses (no previous row, fewer than K candidates, or more
+// than the buffer holds) the row is staged in shared memory and the full
+// radix select runs on it.  Results never depend on which path ran.
 template <typename T>
 __global__ void __launch_bounds__(kWarps * 32)
 topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_stride, int32_t K,
@@ -274,60 +292,103 @@ topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_
     const int64_t r0 = gw * rows_per_warp;
     const int64_t r1 = r0 + rows_per_warp < rows ? r0 + rows_per_warp : rows;
     uint32_t tau_prev = 0;  // threshold key of the previous row (0: none)
+    // margin below the previous threshold, in key steps (scaled for 32-bit keys); adapts to
+    // the density of scores near the threshold: halved when the candidates overflowed the
+    // buffer, doubled when they were fewer than K
+    uint32_t margin = kMargin<Key>;
+    constexpr uint32_t kMarginMin = sizeof(Key) == 2 ? 1u : (1u << 16);
+    constexpr uint32_t kMarginMax = sizeof(Key) == 2 ? 1024u : (1024u << 16);
     for (int64_t row = r0; row < r1; ++row) {
         const T *src = scores + row * row_stride;
         int32_t *orow = out + row * K;
-        const uint32_t t0 = tau_prev > kMargin<Key> ? tau_prev - kMargin<Key> : (tau_prev ? 1u : 0u);
-        int32_t n = 0;
-        for (int32_t base = 0; base < NBp; base += 256) {
-            const int32_t i0 = base + 8 * lane;
-            uint32_t kk[8];
-            load8_keys<T>(src, i0, NB, vec_ok, kk);
-            if constexpr (sizeof(Key) == 2) {
-                uint4 w;
-                w.x = kk[0] | (kk[1] << 16);
-                w.y = kk[2] | (kk[3] << 16);
-                w.z = kk[4] | (kk[5] << 16);
-                w.w = kk[6] | (kk[7] << 16);
-                *reinterpret_cast<uint4 *>(keys + i0) = w;
-            } else {
-                *reinterpret_cast<uint4 *>(keys + i0) = make_uint4(kk[0], kk[1], kk[2], kk[3]);
-                *reinterpret_cast<uint4 *>(keys + i0 + 4) = make_uint4(kk[4], kk[5], kk[6], kk[7]);
-            }
-            if (t0) {
-                uint32_t sel = 0;
-#pragma unroll
-                for (int e = 0; e < 8; ++e) sel |= (kk[e] >= t0 ? 1u : 0u) << e;  // t0 >= 1: excludes key 0
-                const uint32_t ns = (uint32_t)__popc(sel);
-                const uint32_t si = warp_incl_scan(ns, lane);
-                int32_t slot = n + (int32_t)(si - ns);
-                if (sel) {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        if ((sel >> e) & 1u) {
-                            if (slot < kCandCap) {
-                                ckey[slot] = (Key)kk[e];
-                                cidx[slot] = (uint16_t)(i0 + e);
-                            }
-                            ++slot;
-                        }
-                    }
-                }
-                n += (int32_t)__shfl_sync(0xffffffffu, si, 31);
-            }
-        }
-        __syncwarp();
         uint32_t prefix;
         int32_t remaining;
         bool take_all;
-        if (t0 && n >= K && n <= kCandCap) {
-            const int32_t npad = (n + 255) & ~255;
-            for (int32_t i = n + lane; i < npad; i += 32) ckey[i] = Key(0);
+        bool done = false;
+        if (tau_prev) {
+            const uint32_t t0 = tau_prev > kMinFinite<Key> + margin ? tau_prev - margin
+                                                                    : kMinFinite<Key>;
+            const float tf = key_value<T>(t0);  // scores >= tf are candidates (NaN never is)
+            int32_t n = 0;
+            constexpr int VT = 16 / (int)sizeof(T);
+            constexpr int BATCH = 8;  // steps (256 scores each) whose loads are in flight together
+            for (int32_t b0 = 0; b0 < NBp; b0 += 256 * BATCH) {
+                uint4 raw[BATCH][8 / VT];
+#pragma unroll
+                for (int st = 0; st < BATCH; ++st) {
+                    const int32_t i0 = b0 + st * 256 + 8 * lane;
+                    if (vec_ok && i0 + 8 <= NB) {
+#pragma unroll
+                        for (int h = 0; h < 8 / VT; ++h)
+                            raw[st][h] = __ldg(reinterpret_cast<const uint4 *>(src + i0 + h * VT));
+                    }
+                }
+#pragma unroll
+                for (int st = 0; st < BATCH; ++st) {
+                    const int32_t i0 = b0 + st * 256 + 8 * lane;
+                    if (b0 + st * 256 >= NBp) break;
+                    float x[8];
+                    if (vec_ok && i0 + 8 <= NB) {
+#pragma unroll
+                        for (int h = 0; h < 8 / VT; ++h) {
+                            const T *tv = reinterpret_cast<const T *>(&raw[st][h]);
+#pragma unroll
+                            for (int e = 0; e < VT; ++e) x[h * VT + e] = to_f<T>(tv[e]);
+                        }
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) x[e] = (i0 + e < NB) ? to_f<T>(src[i0 + e]) : -INFINITY;
+                    }
+                    uint32_t sel = 0;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) sel |= (x[e] >= tf ? 1u : 0u) << e;
+                    if (__ballot_sync(0xffffffffu, sel != 0u) == 0u) continue;
+                    const uint32_t ns = (uint32_t)__popc(sel);
+                    const uint32_t si = warp_incl_scan(ns, lane);
+                    int32_t slot = n + (int32_t)(si - ns);
+                    for (uint32_t m = sel; m != 0u && slot < kCandCap; m &= m - 1u, ++slot) {
+                        const int e = __ffs(m) - 1;  // only the set bits: 1-2 per lane typically
+                        float xe = x[0];
+#pragma unroll
+                        for (int f = 1; f < 8; ++f) xe = (e == f) ? x[f] : xe;
+                        ckey[slot] = (Key)KeyOf<T>::key(from_f<T>(xe));
+                        cidx[slot] = (uint16_t)(i0 + e);
+                    }
+                    n += (int32_t)__shfl_sync(0xffffffffu, si, 31);
+                }
+            }
             __syncwarp();
-            radix_select<Key, PASSES>(ckey, npad, K, hist, lane, prefix, remaining, take_all);
-            emit_selected(ckey, npad, K, prefix, remaining, take_all,
-                          [&](int32_t i) { return (int32_t)cidx[i]; }, lane, orow);
-        } else {
+            if (n > kCandCap) margin = margin / 2 > kMarginMin ? margin / 2 : kMarginMin;
+            else if (n > kCandCap / 2) margin = margin - margin / 4 > kMarginMin ? margin - margin / 4 : kMarginMin;
+            else if (n < K && t0 > kMinFinite<Key>) margin = margin * 2 < kMarginMax ? margin * 2 : kMarginMax;
+            if (n >= K && n <= kCandCap) {
+                const int32_t npad = (n + 255) & ~255;
+                for (int32_t i = n + lane; i < npad; i += 32) ckey[i] = Key(0);
+                __syncwarp();
+                radix_select<Key, PASSES>(ckey, npad, K, hist, lane, prefix, remaining, take_all);
+                emit_selected(ckey, npad, K, prefix, remaining, take_all,
+                              [&](int32_t i) { return (int32_t)cidx[i]; }, lane, orow);
+                done = true;
+            }
+        }
+        if (!done) {
+            for (int32_t base = 0; base < NBp; base += 256) {
+                const int32_t i0 = base + 8 * lane;
+                uint32_t kk[8];
+                load8_keys<T>(src, i0, NB, vec_ok, kk);
+                if constexpr (sizeof(Key) == 2) {
+                    uint4 w;
+                    w.x = kk[0] | (kk[1] << 16);
+                    w.y = kk[2] | (kk[3] << 16);
+                    w.z = kk[4] | (kk[5] << 16);
+                    w.w = kk[6] | (kk[7] << 16);
+                    *reinterpret_cast<uint4 *>(keys + i0) = w;
+                } else {
+                    *reinterpret_cast<uint4 *>(keys + i0) = make_uint4(kk[0], kk[1], kk[2], kk[3]);
+                    *reinterpret_cast<uint4 *>(keys + i0 + 4) = make_uint4(kk[4], kk[5], kk[6], kk[7]);
+                }
+            }
+            __syncwarp();
             radix_select<Key, PASSES>(keys, NBp, K, hist, lane, prefix, remaining, take_all);
             emit_selected(keys, NB, K, prefix, remaining, take_all, [](int32_t i) { return i; }, lane,
                           orow);
