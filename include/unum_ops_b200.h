@@ -153,7 +153,11 @@ int unum_infllmv2_attn_stage1(const void *q, int64_t T, int64_t Hq, int64_t D, i
  * stride of the stage-1 output), so the pooling never re-reads the scores
  * from HBM.  `out` receives the stage-1 scores as above; `pooled` bf16
  * [Hk, T, NB] receives the block scores (+inf for the init blocks and the
- * local window, -inf for an empty window).  Requires G >= 16.
+ * local window, -inf for an empty window).  Requires G >= 16, and out_stride
+ * must cover every sequence's compressed keys (max_seqlen_k >= each
+ * cu_seqlens_k difference — the reference kernel writes past its rows
+ * otherwise); with a smaller out_stride the pooled result may differ from the
+ * separate pooling call, which then reads neighbouring rows.
  */
 int unum_infllmv2_attn_stage1_pooled(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st,
                                      int64_t q_sh, const void *k, int64_t Tk, int64_t Hk,

@@ -264,3 +264,30 @@ def test_stage1_pooled_equals_stage1_then_pool(spec, dev):
     torch.cuda.synchronize()
     assert torch.equal(s_f, s_r)
     np.testing.assert_array_equal(p_f.float().cpu().numpy(), p_r.float().cpu().numpy())
+
+
+def test_rows_outside_every_sequence(dev, oracle_lib):
+    """Token rows before cu_seqlens_q[0] and after cu_seqlens_q[-1] get the reference's
+    values: zero scores (stage 1) and a pooled row with k_len 0 (pooling)."""
+    from unum_ops_b200.block_select import stage1_pooled
+    from unum_ops_b200.infllm_v2 import infllmv2_attn_stage1, max_pooling_1d_varlen
+
+    rng = np.random.default_rng(91)
+    T, hq, hk = 300, 32, 2
+    q = cases.bf16_round(rng.standard_normal((T, hq, 128), dtype=np.float32))
+    k = cases.bf16_round(rng.standard_normal((40, hk, 128), dtype=np.float32))
+    cu_q = np.array([20, 200, 280], np.int32)
+    cu_k = np.array([0, 11, 40], np.int32)
+    qd, kd = _t(q, dev, torch.bfloat16), _t(k, dev, torch.bfloat16)
+    s = infllmv2_attn_stage1(qd, kd, kd, _t(cu_q, dev), _t(cu_k, dev), max_seqlen_k=29, causal=True)
+    sf, pf = stage1_pooled(qd, kd, _t(cu_q, dev), _t(cu_k, dev), 29, 512, 2, 1)
+    torch.cuda.synchronize()
+    ref = oracle_lib.stage1(q, k, cu_q, cu_k, True, out_stride=128)
+    np.testing.assert_allclose(s.float().cpu().numpy(), ref, atol=ATOL, rtol=RTOL)
+    np.testing.assert_array_equal(s.float().cpu().numpy() == 0, ref == 0)
+    assert torch.equal(s, sf)
+    pr = max_pooling_1d_varlen(s, _t(cu_q, dev), _t(cu_k, dev), torch.zeros(2, dtype=torch.int32, device=dev),
+                               16 * 128, 512, 2, 1)
+    np.testing.assert_array_equal(pf.float().cpu().numpy(), pr.float().cpu().numpy())
+    po = oracle_lib.max_pool(s.float().cpu().numpy(), cu_q, cu_k, np.zeros(2, np.int32), 16 * 128, 512, 2, 1)
+    np.testing.assert_array_equal(pf.float().cpu().numpy(), po)
