@@ -95,29 +95,33 @@ def load_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """nvidia-smi clock / throttle sampling (every 50 ms).  Started before the warm-up
+    so it is running when the timed region begins; summary() keeps only the samples
+    whose timestamps fall inside the timed window [t0, t1] (host wall clock taken
+    after the synchronisations that bracket the region)."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index):
         self.index = index
         self.proc = None
         self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{index}.csv")
 
-    def __enter__(self):
+    def start(self):
         try:
             os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index),
-                 "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                ["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.FIELDS,
                  "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.fh,
                 stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
         return self
 
-    def __exit__(self, *a):
+    def stop(self):
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -126,28 +130,56 @@ class ClockSampler:
                 self.proc.kill()
             self.fh.close()
 
-    def summary(self):
+    def summary(self, t0=None, t1=None):
+        import datetime
+
         if self.proc is None or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm, smax, reasons = [], None, set()
+        sm, smax, reasons, kept = [], None, set(), 0
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in open(self.path):
             f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
+            if len(f) < 10:
                 continue
             try:
-                sm.append(float(f[1]))
-                smax = float(f[2])
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                mhz, mx = float(f[2]), float(f[3])
             except ValueError:
                 continue
-            for n, v in zip(names, f[5:9]):
+            if t0 is not None and not (t0 - 0.05 <= ts <= t1 + 0.05):
+                continue
+            kept += 1
+            sm.append(mhz)
+            smax = mx
+            for n, v in zip(names, f[6:10]):
                 if v.lower() == "active":
                     reasons.add(n)
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": smax, "reasons": sorted(reasons)}
-        loaded = sorted(sm)[len(sm) // 4:] or sm  # drop idle samples at the edges
-        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+            return {"sm_mhz": None, "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": kept}
+
+
+_JSON_FD = None
+
+
+def quiet_stdout():
+    """Route fd 1 (where NCCL and other libraries print banners) to stderr, keeping
+    the original stdout for the one JSON result line."""
+    global _JSON_FD
+    if _JSON_FD is None:
+        sys.stdout.flush()
+        _JSON_FD = os.dup(1)
+        os.dup2(2, 1)
+
+
+def emit(line: dict):
+    text = json.dumps(line) + "\n"
+    if _JSON_FD is not None:
+        os.write(_JSON_FD, text.encode())
+    else:
+        sys.stdout.write(text)
+        sys.stdout.flush()
 
 
 def make_inputs(seed, device):
@@ -187,7 +219,6 @@ def run_ours(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep rank 0's stdout to the one JSON line
         dist.init_process_group("nccl", device_id=dev)
     unum_ops_b200.load()
 
@@ -220,6 +251,7 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize(dev)
 
+    clk = ClockSampler(local).start()
     for _ in range(args.warmup):
         out = step()
     barrier()
@@ -230,13 +262,15 @@ def run_ours(args):
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        barrier()
-        t_start.record(stream)
-        for i in range(args.steps):
-            out = step(evs[i])
-        t_end.record(stream)
-        barrier()
+    barrier()
+    wall0 = time.time()
+    t_start.record(stream)
+    for i in range(args.steps):
+        out = step(evs[i])
+    t_end.record(stream)
+    barrier()
+    wall1 = time.time()
+    clk.stop()
     total_ms = t_start.elapsed_time(t_end)
     per = {"stage1": [], "topk": [], "get_block_table": []}
     for e in evs:
@@ -349,11 +383,11 @@ def run_ours(args):
                     "result": "top-64 block ids int32 [2,131072,64] copied to host"},
             "kernels_api_path": kernels_api,
             "gpu_launches": 4 * args.steps,
-            "clocks": clk.summary(),
+            "clocks": clk.summary(wall0, wall1),
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -375,7 +409,6 @@ def run_decode(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        os.environ.setdefault("NCCL_DEBUG", "WARN")
         dist.init_process_group("nccl", device_id=dev)
     unum_ops_b200.load()
     B = 512
@@ -418,7 +451,7 @@ def run_decode(args):
     kbytes = int(k_lens.sum()) * HK * D * 2
     if rank == 0:
         hbm = load_peaks()[0]
-        print(json.dumps({
+        emit({
             "metric": "decode block selection, sequences/s (512 x 1 query, contexts U[4096,65536])",
             "value": world * B / (ms * 1e-3), "unit": "sequences/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -426,7 +459,7 @@ def run_decode(args):
             "data": "synthetic (seeded)", "config": {"workload": "C4 decode batch",
                                                      "k_cmp_bytes": kbytes},
             "k_cmp_stream_gbs": kbytes / (ms * 1e-3) / 1e9,
-            "k_cmp_stream_frac": kbytes / (ms * 1e-3) / 1e9 / hbm}), flush=True)
+            "k_cmp_stream_frac": kbytes / (ms * 1e-3) / 1e9 / hbm})
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -509,10 +542,11 @@ def run_reference(args):
                          "kind": "port", "sample": steps[0]["sample"]},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def main():
+    quiet_stdout()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=60)
