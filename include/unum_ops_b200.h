@@ -169,6 +169,27 @@ int unum_infllmv2_attn_stage1_pooled(const void *q, int64_t T, int64_t Hq, int64
                                      size_t workspace_bytes, void *stream);
 
 /*
+ * infllmv2_attn_stage1_window — stage 1 (optionally with fused pooling, pooled
+ * may be NULL) restricted to a window of tokens: only query tiles whose tokens
+ * intersect [t_begin, t_end) are computed and written; other rows of `out`
+ * and `pooled` are left as they are.  No single reference function: it lets a
+ * caller stream a long prefill through stage 1 chunk by chunk (for example
+ * overlapping the host-to-device copy of the next chunk's queries), with the
+ * same results as one full call when the chunks cover all tokens.  Tiles are
+ * 256/G tokens of one sequence counted from the sequence start; a window edge
+ * inside a tile computes (and rewrites) the whole tile.
+ */
+int unum_infllmv2_attn_stage1_window(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st,
+                                     int64_t q_sh, const void *k, int64_t Tk, int64_t Hk,
+                                     int64_t k_st, int64_t k_sh, const int32_t *cu_seqlens_q,
+                                     const int32_t *cu_seqlens_k, int64_t n_seq,
+                                     float softmax_scale, int causal, void *out,
+                                     int64_t out_stride, void *pooled, int64_t NB,
+                                     int64_t init_blocks, int64_t local_blocks, int64_t t_begin,
+                                     int64_t t_end, void *workspace, size_t workspace_bytes,
+                                     void *stream);
+
+/*
  * Status word a stage-1 launch leaves in its workspace: 0 = ok; nonzero = a
  * bounded wait inside the kernel gave up (the output is then invalid).  Reads
  * the word with a stream-ordered copy and synchronises the stream.

@@ -291,3 +291,57 @@ def test_rows_outside_every_sequence(dev, oracle_lib):
     np.testing.assert_array_equal(pf.float().cpu().numpy(), pr.float().cpu().numpy())
     po = oracle_lib.max_pool(s.float().cpu().numpy(), cu_q, cu_k, np.zeros(2, np.int32), 16 * 128, 512, 2, 1)
     np.testing.assert_array_equal(pf.float().cpu().numpy(), po)
+
+
+@pytest.mark.parametrize("q_lens,chunk", [([8192], 2048), ([3000, 5000, 17], 1000)],
+                         ids=["single_8k", "varlen_unaligned_chunks"])
+def test_block_select_streamed_equals_block_select(q_lens, chunk, dev):
+    from unum_ops_b200 import block_select, block_select_streamed
+
+    k_lens = [cases.compressed_len(x) for x in q_lens]
+    c = cases.stage1_case("stream", 123, q_lens, k_lens, 32, 2, True)
+    T = sum(q_lens)
+    rng = np.random.default_rng(5)
+    L = max(q_lens)
+    table = rng.permutation(len(q_lens) * L).astype(np.int32).reshape(len(q_lens), L)
+    tb = np.repeat(np.arange(len(q_lens), dtype=np.int32), q_lens)
+    pos = np.concatenate([np.arange(1, n + 1) for n in q_lens]).astype(np.int32)
+    sl = np.array(q_lens, np.int32)
+    q_host = torch.from_numpy(c["q"]).to(torch.bfloat16).pin_memory()
+    k = _t(c["k"], dev, torch.bfloat16)
+    args = [_t(x, dev) for x in (c["cu_q"], c["cu_k"])]
+    rest = [_t(x, dev) for x in (table, tb, pos, sl)]
+    ref = block_select(q_host.to(dev), k, *args, max(k_lens), *rest, max_context_len=L)
+    res_host = torch.empty(2, T, 64, dtype=torch.int32).pin_memory()
+    got = block_select_streamed(q_host, k, *args, max(k_lens), *rest, max_context_len=L,
+                                chunk_tokens=chunk, result_host=res_host)
+    torch.cuda.synchronize()
+    for a, b in zip(ref, got):
+        assert torch.equal(a, b)
+    assert torch.equal(res_host, ref[2].cpu())
+
+
+def test_block_select_streamed_back_to_back(dev):
+    """Several streamed calls issued without synchronising in between must each return
+    the same results (buffers reused across calls are ordered by the streams)."""
+    from unum_ops_b200 import block_select, block_select_streamed
+
+    q_lens = [4096]
+    k_lens = [cases.compressed_len(4096)]
+    c = cases.stage1_case("stream2", 321, q_lens, k_lens, 32, 2, True)
+    table = np.arange(4096, dtype=np.int32).reshape(1, 4096)
+    tb = np.zeros(4096, np.int32)
+    pos = np.arange(1, 4097, dtype=np.int32)
+    sl = np.array([4096], np.int32)
+    k = _t(c["k"], dev, torch.bfloat16)
+    args = [_t(x, dev) for x in (c["cu_q"], c["cu_k"])]
+    rest = [_t(x, dev) for x in (table, tb, pos, sl)]
+    hosts = [torch.from_numpy(c["q"]).to(torch.bfloat16).pin_memory(),
+             (torch.from_numpy(c["q"]) * -1).to(torch.bfloat16).pin_memory()]
+    refs = [block_select(h.to(dev), k, *args, k_lens[0], *rest, max_context_len=4096)[2] for h in hosts]
+    torch.cuda.synchronize()
+    outs = [block_select_streamed(hosts[i % 2], k, *args, k_lens[0], *rest, max_context_len=4096,
+                                  chunk_tokens=512)[2] for i in range(6)]
+    torch.cuda.synchronize()
+    for i, o in enumerate(outs):
+        assert torch.equal(o, refs[i % 2]), i

@@ -7,7 +7,7 @@ plus unum_ops_b200.block_select (top-k and the chained pipeline).
 Kernels live in libunum_ops_b200.so (C ABI: include/unum_ops_b200.h).
 """
 from . import infllm_v2, sparse_kernel_extension  # noqa: F401
-from .block_select import block_select, topk_blocks  # noqa: F401
+from .block_select import block_select, block_select_streamed, topk_blocks  # noqa: F401
 from ._build import build  # noqa: F401
 from ._lib import library_path, load  # noqa: F401
 

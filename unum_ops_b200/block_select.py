@@ -15,7 +15,7 @@ from . import _lib
 from .infllm_v2 import _as_i32, _round_multiple, _workspace, infllmv2_attn_stage1, max_pooling_1d_varlen
 from .sparse_kernel_extension import get_block_table_ref_torch
 
-__all__ = ["topk_blocks", "block_select", "stage1_pooled"]
+__all__ = ["topk_blocks", "block_select", "block_select_streamed", "stage1_pooled"]
 
 
 def stage1_pooled(q, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_k, max_context_len,
@@ -111,4 +111,98 @@ def block_select(q, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_k, block_table
                                        stride)
     idx = topk_blocks(pooled, topk)
     slots = get_block_table_ref_torch(idx, block_table, token_to_bs, token_pos_in_bs, seqlen_q)
+    return scores, pooled, idx, slots
+
+
+def block_select_streamed(q_host, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_k, block_table,
+                          token_to_bs, token_pos_in_bs, seqlen_q, *, max_context_len,
+                          init_blocks=1, local_blocks=2, topk=64, causal=True,
+                          softmax_scale=None, chunk_tokens=16384, result_host=None):
+    """The block-selection path for queries that live in (pinned) host memory.
+
+    The queries are copied to the GPU chunk by chunk on a side stream while the
+    previous chunk runs stage 1 (with fused pooling, restricted to the chunk's
+    tokens), top-k and get_block_table on the current stream, so the
+    host-to-device copy overlaps the compute.  Results equal ``block_select``'s.
+    Everything except ``q_host`` (and ``result_host``) must already be on the
+    GPU.  ``result_host``, if given (pinned int32 [Hk, T, topk]), receives the
+    top-k block ids chunk by chunk, also overlapped.  Returns
+    (scores, pooled, topk_idx, slots) on the GPU.  Needs n_heads / n_kv_heads >= 16
+    and, for full overlap, chunks that are multiples of 256 / G tokens.
+    """
+    dev = _lib.require_cuda(k_cmp, cu_seqlens_q, cu_seqlens_k, block_table)
+    if q_host.device.type != "cpu":
+        raise ValueError("q_host must be a host tensor (pinned for overlap)")
+    T, Hq, D = q_host.shape
+    k = (k_cmp if k_cmp.stride(-1) == 1 else k_cmp.contiguous()).to(torch.bfloat16)
+    Tk, Hk = k.shape[0], k.shape[1]
+    G = Hq // Hk
+    if G < 16:
+        raise NotImplementedError("block_select_streamed needs n_heads / n_kv_heads >= 16")
+    if softmax_scale is None:
+        softmax_scale = D ** (-0.5)
+    B = cu_seqlens_q.numel() - 1
+    cu_q, cu_k = _as_i32(cu_seqlens_q), _as_i32(cu_seqlens_k)
+    W = _round_multiple(int(max_seqlen_k), 128)
+    NB = math.ceil(max_context_len / 64)
+    q = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=dev)
+    scores = torch.empty(Hk, T, W, dtype=torch.bfloat16, device=dev)
+    pooled = torch.empty(Hk, T, NB, dtype=torch.bfloat16, device=dev)
+    idx = torch.empty(Hk, T, topk, dtype=torch.int32, device=dev)
+    slots = torch.empty(T, Hk, topk * 64, dtype=torch.int32, device=dev)
+    L = _lib.load()
+    ws = _workspace(dev, int(L.unum_stage1_workspace_size(B)))
+    comp = torch.cuda.current_stream(dev)
+    copy = torch.cuda.Stream(dev)   # host -> device: query chunks
+    back = torch.cuda.Stream(dev)   # device -> host: top-k ids (PCIe is full duplex)
+    tb = _as_i32(token_to_bs)
+    pos = _as_i32(token_pos_in_bs)
+    sq = _as_i32(seqlen_q)
+    bt = block_table if block_table.dtype == torch.int32 else block_table.to(torch.int32)
+    if bt.stride(1) != 1:
+        bt = bt.contiguous()
+    qsrc = q_host if q_host.dtype == torch.bfloat16 else q_host.to(torch.bfloat16)
+    step = max(int(chunk_tokens) // 128 * 128, 128)
+    bounds = [(a, min(a + step, T)) for a in range(0, T, step)]
+    copied = []
+    # the query buffer may reuse memory that kernels of an earlier call on the compute
+    # stream still read: the copies start only after the compute stream's earlier work
+    copy.wait_stream(comp)
+    q.record_stream(copy)
+    with torch.cuda.stream(copy):
+        for a, b in bounds:
+            q[a:b].copy_(qsrc[a:b], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(copy)
+            copied.append(ev)
+    with torch.cuda.device(dev):
+        for (a, b), ev in zip(bounds, copied):
+            comp.wait_event(ev)
+            rc = L.unum_infllmv2_attn_stage1_window(
+                q.data_ptr(), T, Hq, D, q.stride(0), q.stride(1), k.data_ptr(), Tk, Hk,
+                k.stride(0), k.stride(1), cu_q.data_ptr(), cu_k.data_ptr(), B,
+                float(softmax_scale), int(bool(causal)), scores.data_ptr(), W, pooled.data_ptr(),
+                NB, int(init_blocks), int(local_blocks), a, b, ws.data_ptr(), ws.numel(),
+                comp.cuda_stream)
+            _lib.check(rc)
+            for h in range(Hk):
+                rows = pooled[h, a:b]
+                _lib.check(L.unum_topk_blocks(rows.data_ptr(), _lib.DTYPE_CODES[rows.dtype], b - a, NB,
+                                              NB, int(topk), idx[h, a:b].data_ptr(), comp.cuda_stream))
+            iv = idx[:, a:b]
+            _lib.check(L.unum_get_block_table(
+                iv.data_ptr(), Hk, b - a, topk, iv.stride(0), iv.stride(1), iv.stride(2),
+                bt.data_ptr(), bt.shape[0], bt.shape[1], bt.stride(0), tb[a:b].data_ptr(),
+                pos.data_ptr() if pos.numel() == 1 else pos[a:b].data_ptr(), int(pos.numel() == 1),
+                sq.data_ptr(), int(sq.numel() == 1), 2, slots[a:b].data_ptr(), comp.cuda_stream))
+            if result_host is not None:
+                done = torch.cuda.Event()
+                done.record(comp)
+                back.wait_event(done)
+                idx.record_stream(back)
+                with torch.cuda.stream(back):
+                    for h in range(Hk):
+                        result_host[h, a:b].copy_(idx[h, a:b], non_blocking=True)
+    if result_host is not None:
+        comp.wait_stream(back)
     return scores, pooled, idx, slots

@@ -100,6 +100,8 @@ struct Params {
     // pooled[g][t][j] = max_pooling_1d_varlen(scores, max_seqlen_q = 16*W, cache 0)
     __nv_bfloat16 *pooled;  // [Hk, T, NB] or null
     int32_t NB, init_blocks, local_blocks;
+    // token window: only tiles whose tokens intersect [t_begin, t_end) are computed
+    int64_t t_begin, t_end;
 };
 
 struct Item {
@@ -336,7 +338,7 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
             uint32_t kc = 0, qn = 0;
             for (int64_t w = blockIdx.x; w < n_items; w += gridDim.x) {
                 const Item it = decode<QT>(w, p, cu_tiles, n_tiles);
-                if (it.nkt == 0) continue;
+                if (it.nkt == 0 || it.t0 >= p.t_end || it.t0 + it.nq <= p.t_begin) continue;
                 if (wait_bar(sy, sy.q_empty, (qn & 1) ^ 1, 1)) {
                     mbar_arrive_expect_tx(sy.q_full, kQBytes);
                     tma_load_3d(sbase, &tmQ, 0, it.g * G, (int32_t)it.t0, sy.q_full);
@@ -361,7 +363,7 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
             uint32_t kc = 0, sc = 0, qn = 0;
             for (int64_t w = blockIdx.x; w < n_items; w += gridDim.x) {
                 const Item it = decode<QT>(w, p, cu_tiles, n_tiles);
-                if (it.nkt == 0) continue;
+                if (it.nkt == 0 || it.t0 >= p.t_end || it.t0 + it.nq <= p.t_begin) continue;
                 bool ok = wait_bar(sy, sy.q_full, qn & 1, 3);
                 ++qn;
                 tc_fence_after();
@@ -418,6 +420,7 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         uint32_t sc = 0, stc = 0;
         for (int64_t w = blockIdx.x; w < n_items; w += gridDim.x) {
             const Item it = decode<QT>(w, p, cu_tiles, n_tiles);
+            if (it.t0 >= p.t_end || it.t0 + it.nq <= p.t_begin) continue;  // outside the token window
             named_bar_sync(kEpiBarrier, kEpiWarps * 32);  // previous tile done with lim_s/stats
             if (tid < QT)
                 lim_s[tid] = tid < it.nq ? visible(it.local0 + tid, it.q_len, it.k_len, p.causal) : 0;
@@ -813,7 +816,7 @@ int stage1_run(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, in
                const int32_t *cu_seqlens_q, const int32_t *cu_seqlens_k, int64_t n_seq,
                float softmax_scale, int causal, void *out, int64_t out_stride, void *workspace,
                size_t workspace_bytes, void *stream, void *pooled, int64_t NB, int64_t init_blocks,
-               int64_t local_blocks) {
+               int64_t local_blocks, int64_t t_begin = 0, int64_t t_end = INT64_MAX) {
     UNUM_CHECK_ARG(T >= 0 && Tk >= 0 && Hq > 0 && Hk > 0 && n_seq >= 0 && out_stride >= 0,
                    "bad sizes");
     UNUM_CHECK_ARG(Hq % Hk == 0, "n_heads (%lld) must be a multiple of n_kv_heads (%lld)",
@@ -894,6 +897,8 @@ int stage1_run(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, in
     p.NB = (int32_t)NB;
     p.init_blocks = (int32_t)init_blocks;
     p.local_blocks = (int32_t)local_blocks;
+    p.t_begin = t_begin;
+    p.t_end = t_end;
     switch (G) {
         case 2: return launch_main<2>(mq, mk, mo, p, T, s);
         case 4: return launch_main<4>(mq, mk, mo, p, T, s);
@@ -946,6 +951,27 @@ extern "C" int unum_stage1_status(const void *workspace, void *stream, int32_t *
     UNUM_CHECK_CUDA(cudaMemcpyAsync(status_out, workspace, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
     UNUM_CHECK_CUDA(cudaStreamSynchronize(s));
     return UNUM_OK;
+}
+
+extern "C" int unum_infllmv2_attn_stage1_window(
+    const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, int64_t q_sh, const void *k,
+    int64_t Tk, int64_t Hk, int64_t k_st, int64_t k_sh, const int32_t *cu_seqlens_q,
+    const int32_t *cu_seqlens_k, int64_t n_seq, float softmax_scale, int causal, void *out,
+    int64_t out_stride, void *pooled, int64_t NB, int64_t init_blocks, int64_t local_blocks,
+    int64_t t_begin, int64_t t_end, void *workspace, size_t workspace_bytes, void *stream) {
+    unum::clear_error();
+    UNUM_CHECK_ARG(t_begin >= 0 && t_end >= t_begin, "bad token window [%lld, %lld)",
+                   (long long)t_begin, (long long)t_end);
+    if (pooled) {
+        UNUM_CHECK_ARG(NB > 0 && NB < (int64_t)1 << 30, "pooled output needs 0 < NB < 2^30");
+        if (Hk <= 0 || Hq % Hk != 0 || Hq / Hk < 16) {
+            unum::set_error("fused pooling needs a head group of at least 16");
+            return UNUM_ERR_UNSUPPORTED;
+        }
+    }
+    return stage1_run(q, T, Hq, D, q_st, q_sh, k, Tk, Hk, k_st, k_sh, cu_seqlens_q, cu_seqlens_k,
+                      n_seq, softmax_scale, causal, out, out_stride, workspace, workspace_bytes,
+                      stream, pooled, pooled ? NB : 0, init_blocks, local_blocks, t_begin, t_end);
 }
 
 // ------------------------------------------------------------------ allocation-free variant
