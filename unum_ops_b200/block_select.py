@@ -163,7 +163,9 @@ def block_select_streamed(q_host, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_
         bt = bt.contiguous()
     qsrc = q_host if q_host.dtype == torch.bfloat16 else q_host.to(torch.bfloat16)
     step = max(int(chunk_tokens) // 128 * 128, 128)
-    bounds = [(a, min(a + step, T)) for a in range(0, T, step)]
+    # last chunks first: with causal masking the late tokens cost the most, so the
+    # cheapest chunk is the one left exposed after the final copy
+    bounds = [(a, min(a + step, T)) for a in range(0, T, step)][::-1]
     copied = []
     # the query buffer may reuse memory that kernels of an earlier call on the compute
     # stream still read: the copies start only after the compute stream's earlier work
