@@ -54,7 +54,8 @@ constexpr int kStages = 4;         // K ring depth
 constexpr int kEpiWarps = 16;      // 4 warpgroups, 64 accumulator columns each
 constexpr int kProducerWarp = 16;
 constexpr int kMmaWarp = 17;
-constexpr int kThreads = (kEpiWarps + 2) * 32;
+constexpr int kFillWarp = 18;       // writes what lies past each item's computed key tiles
+constexpr int kThreads = (kEpiWarps + 3) * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kEpiBarrier = 1;     // named barrier id for the 256 epilogue threads
 
@@ -275,10 +276,66 @@ __device__ __forceinline__ void p2_chunk(const float (&v)[32], uint64_t (&acc)[6
 #undef UNUM_P2
 }
 
+// Everything of an item past its computed key tiles: zero scores from column
+// nkt*128 on, and the pooled blocks whose windows hold only those keys (zeros
+// inside k_len, an empty window -inf past it, +inf on init/local blocks).  These
+// regions are disjoint from every store of the epilogue warps, so this warp runs
+// on its own, without barriers.
+template <int QT>
+__device__ __noinline__ void fill_tails(const Params &p, const int32_t *cu_tiles, int32_t n_tiles,
+                                      int64_t n_items, int lane) {
+    const bool vec_pool = p.pooled != nullptr && (p.NB & 7) == 0 &&
+                          (reinterpret_cast<uintptr_t>(p.pooled) & 15) == 0;
+    for (int64_t w = blockIdx.x; w < n_items; w += gridDim.x) {
+        const Item it = decode<QT>(w, p, cu_tiles, n_tiles);
+        if (it.t0 >= p.t_end || it.t0 + it.nq <= p.t_begin) continue;
+        const int32_t c0 = it.nkt * kBN;
+        const int32_t n16 = (int32_t)((p.out_stride - c0) >> 3);  // 16-byte chunks a row
+        const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+        for (int32_t tq = 0; tq < it.nq && n16 > 0; ++tq) {
+            uint4 *dst = reinterpret_cast<uint4 *>(
+                p.out + ((int64_t)it.g * p.T + it.t0 + tq) * p.out_stride + c0);
+            for (int32_t e = lane; e < n16; e += 32) __stcs(dst + e, z4);
+        }
+        if (p.pooled == nullptr) continue;
+        const int32_t jstart = it.nkt > 0 ? it.nkt * 32 + 1 : 0;
+        const int32_t jhas = (it.k_len + 4) / 4;  // blocks jg < jhas have 4*jg-1 < k_len
+        for (int32_t tq = 0; tq < it.nq && jstart < p.NB; ++tq) {
+            const int32_t off_bq = (it.local0 + tq) / 64;
+            __nv_bfloat16 *prow = p.pooled + ((int64_t)it.g * p.T + it.t0 + tq) * p.NB;
+            auto value = [&](int32_t jg) -> uint16_t {
+                const bool minf = jg < p.init_blocks || (off_bq >= jg && off_bq <= jg + p.local_blocks);
+                return minf ? 0x7F80u : (jg < jhas ? 0x0000u : 0xFF80u);
+            };
+            int32_t jv = vec_pool ? ((jstart + 7) & ~7) : p.NB;  // first 8-aligned block
+            if (jv > p.NB) jv = p.NB;
+            for (int32_t jg = jstart + lane; jg < jv; jg += 32)
+                reinterpret_cast<uint16_t *>(prow)[jg] = value(jg);
+            for (int32_t j0 = jv + 8 * lane; j0 < p.NB; j0 += 256) {
+                const bool no_mask = j0 >= p.init_blocks &&
+                                     (p.local_blocks < 0 || off_bq < j0 || off_bq - p.local_blocks > j0 + 7);
+                uint4 v;
+                if (no_mask && j0 + 7 < jhas) {
+                    v = z4;
+                } else if (no_mask && j0 >= jhas) {
+                    v = make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);
+                } else {
+                    uint32_t h[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        h[i] = (uint32_t)value(j0 + 2 * i) | ((uint32_t)value(j0 + 2 * i + 1) << 16);
+                    v = make_uint4(h[0], h[1], h[2], h[3]);
+                }
+                *reinterpret_cast<uint4 *>(prow + j0) = v;
+            }
+        }
+    }
+}
+
 template <int G>
-__global__ void __launch_bounds__(kThreads, 1)  // 18 warps: at most 96 registers a thread
+__global__ void __launch_bounds__(kThreads, 1)  // 19 warps, 5 on some schedulers: at most 96 registers a thread
 stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-              const __grid_constant__ CUtensorMap tmO, const Params p) {
+              const __grid_constant__ CUtensorMap tmO, const __grid_constant__ Params p) {
     constexpr int QT = kRows / G;  // tokens per tile
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -403,6 +460,8 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                 if (ok) umma_commit(sy.q_empty);
             }
         }
+    } else if (warp == kFillWarp) {
+        fill_tails<QT>(p, cu_tiles, n_tiles, n_items, lane);
     } else {
         // ------------------------------------------------------------ epilogue
         // 16 warps = 4 warpgroups; warp w reads TMEM lanes 32*(w%4)..+31.
@@ -420,7 +479,8 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         uint32_t sc = 0, stc = 0;
         for (int64_t w = blockIdx.x; w < n_items; w += gridDim.x) {
             const Item it = decode<QT>(w, p, cu_tiles, n_tiles);
-            if (it.t0 >= p.t_end || it.t0 + it.nq <= p.t_begin) continue;  // outside the token window
+            // nothing to compute (the fill warp writes such rows) or outside the token window
+            if (it.nkt == 0 || it.t0 >= p.t_end || it.t0 + it.nq <= p.t_begin) continue;
             named_bar_sync(kEpiBarrier, kEpiWarps * 32);  // previous tile done with lim_s/stats
             if (tid < QT)
                 lim_s[tid] = tid < it.nq ? visible(it.local0 + tid, it.q_len, it.k_len, p.causal) : 0;
@@ -496,7 +556,14 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                 const int tq0 = col0 / G;
                 const ulonglong2 *st4 = reinterpret_cast<const ulonglong2 *>(stats + col0);  // -b, 4 at a time
                 const uint32_t tcol2 = lane_base + col0;
-                float halo = -INFINITY;  // previous tile's last key, for fused pooling
+                // fused pooling: warp wq pools token tq0 + wq (a pooled launch has G >= 16, so
+                // NQ <= 4); the row pointer and the token's local-block window are per item
+                const int32_t ptq = tq0 + wq;
+                const bool pool_w = p.pooled != nullptr && wq < NQ && ptq < it.nq;
+                __nv_bfloat16 *prow = p.pooled + ((int64_t)it.g * p.T + it.t0 + ptq) * p.NB;
+                const int32_t off_bq = (it.local0 + ptq) / 64;
+                float halo = -INFINITY;  // previous tile's last key (slow path)
+                uint32_t halo_b = 0;     // the same as bf16 bits (fast path)
                 const bool wg_idle2 = tq0 >= it.nq;  // every token of this warpgroup is past the end
                 for (int32_t kt = 0; wg_idle2 && kt < it.nkt; ++kt, ++sc) {
                     const uint32_t buf = sc & 1;
@@ -573,19 +640,33 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                                     out_g[(it.t0 + tq) * p.out_stride + col] = stg[e];
                             }
                         }
-                        if (p.pooled) {
-                            // warp wq pools token tq0+wq: lane = block in this tile, its window is
-                            // keys [4*lane-1, 4*lane+3]; key 4*lane-1 is the previous lane's last
-                            // key (shuffle) or, for lane 0, the previous tile's last key (halo)
-                            for (int qi = wq; qi < NQ; qi += 4) {
-                                const int tq = tq0 + qi;
-                                const uint2 raw = *reinterpret_cast<const uint2 *>(stg + qi * kBN + 4 * lane);
+                        if (pool_w) {
+                            // lane = block jg of this tile; its window is keys [4*lane-1, 4*lane+3],
+                            // key 4*lane-1 being the previous lane's last key (shuffle) or, for
+                            // lane 0, the previous tile's last key (halo)
+                            const uint2 raw = *reinterpret_cast<const uint2 *>(stg + wq * kBN + 4 * lane);
+                            const int32_t jg = kt * 32 + lane;
+                            const bool minf = jg < p.init_blocks || (off_bq >= jg && off_bq <= jg + p.local_blocks);
+                            if (kt > 0 && kt + 1 < it.nkt && kt * kBN + kBN <= it.k_len) {
+                                // interior tile: every window key exists and every staged score is
+                                // finite and >= 0, so the max is the largest bf16 bit pattern
+                                const uint32_t up = raw.y >> 16;
+                                uint32_t left = __shfl_up_sync(0xffffffffu, up, 1);
+                                if (lane == 0) left = halo_b;
+                                halo_b = __shfl_sync(0xffffffffu, up, 31);
+                                halo = __uint_as_float(halo_b << 16);
+                                const uint32_t m2 = __vmaxu2(__vmaxu2(raw.x, raw.y), left | (left << 16));
+                                const uint32_t mx = max(m2 & 0xffffu, m2 >> 16);
+                                if (jg < p.NB)
+                                    reinterpret_cast<uint16_t *>(prow)[jg] = minf ? (uint16_t)0x7F80u : (uint16_t)mx;
+                            } else {
                                 const __nv_bfloat162 lo2 = *reinterpret_cast<const __nv_bfloat162 *>(&raw.x);
                                 const __nv_bfloat162 hi2 = *reinterpret_cast<const __nv_bfloat162 *>(&raw.y);
                                 float x[4] = {__low2float(lo2), __high2float(lo2), __low2float(hi2), __high2float(hi2)};
                                 float left = __shfl_up_sync(0xffffffffu, x[3], 1);
                                 if (lane == 0) left = halo;
                                 halo = __shfl_sync(0xffffffffu, x[3], 31);
+                                halo_b = __float_as_uint(halo) >> 16;
                                 const int32_t c0k = kt * kBN + 4 * lane;  // global key of x[0]
                                 if (c0k + 3 >= it.k_len || c0k == 0) {
 #pragma unroll
@@ -594,25 +675,19 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                                     if (c0k - 1 < 0 || c0k - 1 >= it.k_len) left = -INFINITY;
                                 }
                                 const float mx = fmaxf(fmax3(left, x[0], x[1]), fmaxf(x[2], x[3]));
-                                if (tq < it.nq) {
-                                    const int32_t jg = kt * 32 + lane;
-                                    const int32_t off_bq = (it.local0 + tq) / 64;
-                                    __nv_bfloat16 *prow = p.pooled + ((int64_t)it.g * p.T + it.t0 + tq) * p.NB;
-                                    if (jg < p.NB) {
-                                        const bool minf = jg < p.init_blocks || (off_bq >= jg && off_bq <= jg + p.local_blocks);
-                                        const bool has = 4 * jg - 1 < it.k_len;
-                                        prow[jg] = __float2bfloat16_rn(minf ? INFINITY : (has ? mx : -INFINITY));
-                                    }
-                                    if (lane == 31 && kt + 1 == it.nkt && jg + 1 < p.NB) {
-                                        // first block past the computed tiles: key 128*nkt-1 plus zeros
-                                        const int32_t jn = jg + 1, cl = kt * kBN + kBN - 1;
-                                        float m2 = -INFINITY;
-                                        if (cl < it.k_len) m2 = x[3];
-                                        if (cl + 1 < it.k_len) m2 = fmaxf(m2, 0.f);
-                                        const bool minf = jn < p.init_blocks || (off_bq >= jn && off_bq <= jn + p.local_blocks);
-                                        const bool has = 4 * jn - 1 < it.k_len;
-                                        prow[jn] = __float2bfloat16_rn(minf ? INFINITY : (has ? m2 : -INFINITY));
-                                    }
+                                if (jg < p.NB) {
+                                    const bool has = 4 * jg - 1 < it.k_len;
+                                    prow[jg] = __float2bfloat16_rn(minf ? INFINITY : (has ? mx : -INFINITY));
+                                }
+                                if (lane == 31 && kt + 1 == it.nkt && jg + 1 < p.NB) {
+                                    // first block past the computed tiles: key 128*nkt-1 plus zeros
+                                    const int32_t jn = jg + 1, cl = kt * kBN + kBN - 1;
+                                    float m2 = -INFINITY;
+                                    if (cl < it.k_len) m2 = x[3];
+                                    if (cl + 1 < it.k_len) m2 = fmaxf(m2, 0.f);
+                                    const bool minf2 = jn < p.init_blocks || (off_bq >= jn && off_bq <= jn + p.local_blocks);
+                                    const bool has = 4 * jn - 1 < it.k_len;
+                                    prow[jn] = __float2bfloat16_rn(minf2 ? INFINITY : (has ? m2 : -INFINITY));
                                 }
                             }
                         }
@@ -629,37 +704,6 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                                 const float o = j < lim_s[tq] ? fmaxf(a, 0.f) : 0.f;
                                 out_g[(it.t0 + tq) * p.out_stride + j] = __float2bfloat16_rn(o);
                             }
-                        }
-                    }
-                }
-            }
-            // ---------------- zero the columns past the computed key tiles
-            {
-                const int64_t c0 = (int64_t)it.nkt * kBN;
-                const int64_t ncol = p.out_stride - c0;
-                if (ncol > 0) {
-                    const int64_t per_row = ncol / 8;  // 16-byte chunks (out_stride % 128 == 0)
-                    const int64_t total = per_row * it.nq;
-                    const uint4 z = make_uint4(0, 0, 0, 0);
-                    for (int64_t e = tid; e < total; e += kEpiWarps * 32) {
-                        const int64_t tq = e / per_row, cc = e - tq * per_row;
-                        uint4 *dst = reinterpret_cast<uint4 *>(out_g + (it.t0 + tq) * p.out_stride + c0) + cc;
-                        *dst = z;
-                    }
-                }
-                if (p.pooled) {
-                    // blocks whose windows hold only keys past the computed tiles: zeros while
-                    // inside k_len, else an empty window (-inf); +inf where init/local masks
-                    const int32_t jstart = it.nkt > 0 ? it.nkt * 32 + 1 : 0;
-                    const int32_t nj = p.NB - jstart;
-                    if (nj > 0) {
-                        for (int64_t e = tid; e < (int64_t)nj * it.nq; e += kEpiWarps * 32) {
-                            const int32_t tq = (int32_t)(e / nj), jg = jstart + (int32_t)(e - (int64_t)tq * nj);
-                            const int32_t off_bq = (it.local0 + tq) / 64;
-                            const bool minf = jg < p.init_blocks || (off_bq >= jg && off_bq <= jg + p.local_blocks);
-                            const bool has = 4 * jg - 1 < it.k_len;
-                            p.pooled[((int64_t)it.g * p.T + it.t0 + tq) * p.NB + jg] =
-                                __float2bfloat16_rn(minf ? INFINITY : (has ? 0.f : -INFINITY));
                         }
                     }
                 }
