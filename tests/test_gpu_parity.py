@@ -149,6 +149,44 @@ def test_topk_vs_oracle(kw, dtype, dev, oracle_lib):
     np.testing.assert_array_equal(out.cpu().numpy(), ref)
 
 
+def _similar_rows(seed, rows, NB, kind):
+    """Runs of neighbouring rows that differ a little, like pooled scores of
+    consecutive tokens: each warp of the top-k kernel then reuses the previous
+    row's threshold (the candidate path), with shifts that force the fallback."""
+    rng = np.random.default_rng(seed)
+    base = rng.standard_normal(NB).astype(np.float32)
+    drift = np.cumsum(rng.standard_normal((rows, 1)).astype(np.float32) * 0.01, axis=0)
+    x = base[None, :] + 0.05 * rng.standard_normal((rows, NB)).astype(np.float32) + drift
+    if kind == "ties":
+        x = np.round(x * 4) / 4
+    if kind == "jumps":  # the distribution moves every 500 rows
+        x += (np.arange(rows) // 500 % 3)[:, None].astype(np.float32) * 2.0
+    if kind == "cluster":  # winners concentrated in the positions one lane loads
+        hot = (np.arange(NB) % 256) < 8
+        x[:, hot] += 3.0
+    if kind == "masks":
+        x[rng.random(x.shape) < 0.002] = np.inf
+        x[rng.random(x.shape) < 0.001] = np.nan
+        cut = rng.integers(NB // 2, NB + 1, size=rows)
+        x[np.arange(NB)[None, :] >= cut[:, None]] = -np.inf
+    return x
+
+
+@pytest.mark.parametrize("NB,K,kind", [
+    (2048, 64, "plain"), (2048, 64, "masks"), (2048, 64, "ties"), (2048, 64, "jumps"),
+    (2048, 64, "cluster"), (4096, 128, "ties"), (1000, 64, "masks"), (300, 7, "plain"),
+], ids=lambda v: str(v))
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_topk_runs_of_similar_rows(NB, K, kind, dtype, dev, oracle_lib):
+    from unum_ops_b200 import topk_blocks
+
+    rows = 24000 if NB <= 2048 else 12000
+    x = _t(_similar_rows(7, rows, NB, kind), dev, dtype)
+    out = topk_blocks(x, K)
+    ref = oracle_lib.topk(x.float().cpu().numpy(), K)
+    np.testing.assert_array_equal(out.cpu().numpy(), ref)
+
+
 # ---------------------------------------------------------------- stage 1
 def _stage1(c, dev):
     from unum_ops_b200.infllm_v2 import infllmv2_attn_stage1

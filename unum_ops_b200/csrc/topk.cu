@@ -33,13 +33,9 @@ constexpr int kMaxK = 1024;
 
 template <typename T> __device__ __forceinline__ float to_f(T v);
 template <> __device__ __forceinline__ float to_f<float>(float v) { return v; }
-template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
-template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
 
 template <typename T> __device__ __forceinline__ T from_f(float v);
 template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
-template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
-template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
 
 // Order-preserving keys: larger score -> larger key; -inf and NaN -> 0.
 template <typename T> struct KeyOf;
@@ -82,10 +78,6 @@ __device__ __forceinline__ uint32_t warp_incl_scan(uint32_t x, int lane) {
     return x;
 }
 
-// Radix select of the K-th largest key among keys[0, n_pad) (n_pad a multiple
-// of 256; key 0 = not a candidate).  Returns the threshold key in `prefix` and
-// in `remaining` how many keys equal to it are taken (lowest index first);
-// take_all when there are at most K candidates.
 // 8 consecutive keys from shared memory (i0 a multiple of 8) with 16-byte loads.
 template <typename Key>
 __device__ __forceinline__ void load8(const Key *keys, int32_t i0, uint32_t (&k)[8]) {
@@ -111,10 +103,41 @@ __host__ __device__ constexpr size_t warp_smem_bytes(int64_t NB) {
     return 1024 + ((NB + 255) / 256 * 256) * sizeof(Key) + 512 * sizeof(Key) + 512 * 2;
 }
 
-template <typename Key, int PASSES>
-__device__ __forceinline__ void radix_select(const Key *keys, int32_t n_pad, int32_t K, uint32_t *hist,
-                                             int lane, uint32_t &prefix, int32_t &remaining,
-                                             bool &take_all) {
+// Histogram of the staged keys[0, n_pad) whose bits under pmask equal prefix, by
+// the digit at `shift`: run-length aggregated atomics (neighbouring keys of a
+// lane often share a digit).
+template <typename Key>
+__device__ __forceinline__ void hist_staged(const Key *keys, int32_t n_pad, uint32_t *hist, int lane,
+                                            uint32_t pmask, uint32_t prefix, int shift) {
+    for (int32_t base = 0; base < n_pad; base += 256) {
+        const int32_t i0 = base + 8 * lane;
+        uint32_t kk[8];
+        load8(keys, i0, kk);
+        uint32_t run_d = 256u, run_c = 0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const uint32_t k = kk[e];
+            const bool m = k != 0u && (k & pmask) == prefix;
+            const uint32_t d = m ? ((k >> shift) & 255u) : 256u;
+            if (d != run_d) {
+                if (run_c) atomicAdd(&hist[run_d], run_c);
+                run_d = d;
+                run_c = 0;
+            }
+            run_c += m ? 1u : 0u;
+        }
+        if (run_c) atomicAdd(&hist[run_d], run_c);
+    }
+}
+
+// Radix select of the K-th largest among a warp's keys (key 0 = not a
+// candidate), 8-bit digits from the top; fill(pmask, prefix, shift) adds the
+// keys matching the prefix so far to the histogram.  Returns the threshold key
+// in `prefix` and in `remaining` how many keys equal to it are taken (lowest
+// index first); take_all when there are at most K candidates.
+template <typename Key, int PASSES, typename Fill>
+__device__ __forceinline__ void radix_select_with(Fill fill, int32_t K, uint32_t *hist, int lane,
+                                                  uint32_t &prefix, int32_t &remaining, bool &take_all) {
     constexpr int KB = 8 * (int)sizeof(Key);
     prefix = 0;
     uint32_t pmask = 0;
@@ -123,28 +146,10 @@ __device__ __forceinline__ void radix_select(const Key *keys, int32_t n_pad, int
 #pragma unroll 1
     for (int p = 0; p < PASSES; ++p) {
         const int shift = KB - 8 - 8 * p;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) hist[lane * 8 + i] = 0;
+        reinterpret_cast<uint4 *>(hist)[2 * lane] = make_uint4(0u, 0u, 0u, 0u);
+        reinterpret_cast<uint4 *>(hist)[2 * lane + 1] = make_uint4(0u, 0u, 0u, 0u);
         __syncwarp();
-        for (int32_t base = 0; base < n_pad; base += 256) {
-            const int32_t i0 = base + 8 * lane;
-            uint32_t kk[8];
-            load8(keys, i0, kk);
-            uint32_t run_d = 256u, run_c = 0;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const uint32_t k = kk[e];
-                const bool m = k != 0u && (k & pmask) == prefix;
-                const uint32_t d = m ? ((k >> shift) & 255u) : 256u;
-                if (d != run_d) {
-                    if (run_c) atomicAdd(&hist[run_d], run_c);
-                    run_d = d;
-                    run_c = 0;
-                }
-                run_c += m ? 1u : 0u;
-            }
-            if (run_c) atomicAdd(&hist[run_d], run_c);
-        }
+        fill(pmask, prefix, shift);
         __syncwarp();
         uint32_t c[8];
         uint32_t s = 0;
@@ -183,6 +188,84 @@ __device__ __forceinline__ void radix_select(const Key *keys, int32_t n_pad, int
         pmask |= 255u << shift;
         __syncwarp();
     }
+}
+
+template <typename Key, int PASSES>
+__device__ __forceinline__ void radix_select(const Key *keys, int32_t n_pad, int32_t K, uint32_t *hist,
+                                             int lane, uint32_t &prefix, int32_t &remaining,
+                                             bool &take_all) {
+    radix_select_with<Key, PASSES>(
+        [&](uint32_t pmask, uint32_t pre, int shift) { hist_staged(keys, n_pad, hist, lane, pmask, pre, shift); },
+        K, hist, lane, prefix, remaining, take_all);
+}
+
+// K-th largest among the lane-private candidate keys (slot j of lane l at
+// l + 32*j, `mine` slots this lane).  One histogram pass over keys offset from
+// `base`: bins 1..254 hold single keys, bin 0 everything <= base, bin 255
+// everything >= base + 255, so when the K-th largest lands in bins 1..254 it is
+// exact; otherwise the 8-bit radix select settles it.  Same outputs as
+// radix_select_with.
+template <typename Key, int PASSES>
+__device__ __forceinline__ void select_stored(const Key *ckey, uint32_t mine, uint32_t base, int32_t K,
+                                              uint32_t *hist, int lane, uint32_t &prefix,
+                                              int32_t &remaining, bool &take_all) {
+    reinterpret_cast<uint4 *>(hist)[2 * lane] = make_uint4(0u, 0u, 0u, 0u);
+    reinterpret_cast<uint4 *>(hist)[2 * lane + 1] = make_uint4(0u, 0u, 0u, 0u);
+    __syncwarp();
+    for (uint32_t j = 0; j < mine; ++j) {
+        const uint32_t k = ckey[lane + 32 * j];
+        const uint32_t d = k <= base ? 0u : (k - base < 255u ? k - base : 255u);
+        atomicAdd(&hist[d], 1u);
+    }
+    __syncwarp();
+    uint32_t c[8];
+    uint32_t sum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {  // lane owns bins 255-8*lane-i (descending)
+        c[i] = hist[255 - 8 * lane - i];
+        sum += c[i];
+    }
+    const uint32_t incl = warp_incl_scan(sum, lane);
+    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+    __syncwarp();
+    if (total <= (uint32_t)K) {
+        prefix = 0;
+        remaining = K;
+        take_all = true;
+        return;
+    }
+    const uint32_t excl = incl - sum;
+    const bool own = excl < (uint32_t)K && (uint32_t)K <= incl;
+    const uint32_t owner = __ffs(__ballot_sync(0xffffffffu, own)) - 1;
+    uint32_t digit = 0, above = 0;
+    if (own) {
+        uint32_t run = excl;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (run + c[i] >= (uint32_t)K) {
+                digit = 255u - 8u * lane - i;
+                above = run;
+                break;
+            }
+            run += c[i];
+        }
+    }
+    digit = __shfl_sync(0xffffffffu, digit, owner);
+    above = __shfl_sync(0xffffffffu, above, owner);
+    if (digit != 0u && digit != 255u) {
+        prefix = base + digit;
+        remaining = K - (int32_t)above;
+        take_all = false;
+        return;
+    }
+    radix_select_with<Key, PASSES>(
+        [&](uint32_t pmask, uint32_t pre, int shift) {
+            for (uint32_t j = 0; j < mine; ++j) {
+                const uint32_t k = ckey[lane + 32 * j];
+                if ((k & pmask) == pre) atomicAdd(&hist[(k >> shift) & 255u], 1u);
+            }
+        },
+        K, hist, lane, prefix, remaining, take_all);
 }
 
 // Write the selected entries of keys[0, n) in index order to orow[0, K), then
@@ -227,9 +310,93 @@ constexpr int kCandCap = 512;   // candidate buffer per warp
 // threshold margin in key steps: 32 bf16/fp16 steps (bf16: 2^(32/128) = 19 % in value);
 // the same relative width for 32-bit keys
 template <typename Key> constexpr uint32_t kMargin = sizeof(Key) == 2 ? 32u : (32u << 16);
-// key of the most negative finite score: the candidate bound never goes below it,
-// so -inf (and NaN) scores are never counted as candidates
-template <typename Key> constexpr uint32_t kMinFinite = sizeof(Key) == 2 ? 0x80u : 0x00800000u;
+// key of the most negative finite score (bf16 0xFF7F, fp16 0xFBFF, fp32
+// 0xFF7FFFFF): the candidate bound never goes below it, so -inf (and NaN) scores
+// are never counted as candidates
+template <typename T> constexpr uint32_t kMinFinite = 0x00800000u;
+template <> constexpr uint32_t kMinFinite<__nv_bfloat16> = 0x0080u;
+template <> constexpr uint32_t kMinFinite<__half> = 0x0400u;
+
+constexpr int kLaneCand = kCandCap / 32;  // candidate slots of one lane (16-bit path)
+
+// "x >= t" on two packed 16-bit scores: 0xFFFF in each half where true (NaN: false).
+template <typename T> __device__ __forceinline__ uint32_t ge2(uint32_t x, uint32_t t2);
+template <> __device__ __forceinline__ uint32_t ge2<__nv_bfloat16>(uint32_t x, uint32_t t2) {
+    return __hge2_mask(*reinterpret_cast<const __nv_bfloat162 *>(&x), *reinterpret_cast<const __nv_bfloat162 *>(&t2));
+}
+template <> __device__ __forceinline__ uint32_t ge2<__half>(uint32_t x, uint32_t t2) {
+    return __hge2_mask(*reinterpret_cast<const __half2 *>(&x), *reinterpret_cast<const __half2 *>(&t2));
+}
+// "x == t" likewise (bit-pattern equality: keys are not NaN, and +0/-0 have distinct keys)
+template <typename T> __device__ __forceinline__ uint32_t eq2(uint32_t x, uint32_t t2) {
+    return __vcmpeq2(x, t2);
+}
+// -inf bit pattern: fill for positions past the row end
+template <typename T> constexpr uint32_t kNegInf16 = 0xFF80u;
+template <> constexpr uint32_t kNegInf16<__half> = 0xFC00u;
+template <typename T> __device__ __forceinline__ uint32_t bits16(T v) {
+    return (uint32_t)(*reinterpret_cast<const uint16_t *>(&v));
+}
+// key of a 16-bit score that is neither NaN nor -inf, from its bits, and back
+__device__ __forceinline__ uint32_t key16_bits(uint32_t u) {
+    return (u & 0x8000u) ? (~u & 0xFFFFu) : (u | 0x8000u);
+}
+__device__ __forceinline__ uint32_t key_bits16(uint32_t k) {
+    return (k & 0x8000u) ? (k & 0x7FFFu) : (~k & 0xFFFFu);
+}
+
+// 8 scores from i0 as packed bits, -inf past the row end (unaligned rows, row tail);
+// kept out of line so the unrolled vector path stays small in the instruction cache.
+template <typename T>
+__device__ __noinline__ uint4 load8_bits_slow(const T *src, int32_t i0, int32_t NB) {
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const uint32_t lo = i0 + 2 * e < NB ? bits16(src[i0 + 2 * e]) : kNegInf16<T>;
+        const uint32_t hv = i0 + 2 * e + 1 < NB ? bits16(src[i0 + 2 * e + 1]) : kNegInf16<T>;
+        w[e] = lo | (hv << 16);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Emit from bitmaps over block ids: sel = blocks taken outright, tie = blocks whose
+// key equals the threshold, of which the `remaining` lowest ids are taken; a third
+// bitmap eqw is ignored (eq_mode 0), replaces the ties (1) or is taken whole (2).
+// Lane l sweeps a contiguous run of words, so ids come out ascending; then -1
+// padding.
+__device__ __forceinline__ void emit_bitmap(const uint32_t *selw, const uint32_t *tiew, const uint32_t *eqw,
+                                            int eq_mode, int32_t nw, int32_t K, int32_t remaining,
+                                            int lane, int32_t *orow) {
+    constexpr int kMaxW = kMaxNB / 32 / 32;  // words a lane sweeps at most
+    const int32_t wpl = (nw + 31) >> 5;
+    const int32_t w0 = lane * wpl;
+    uint32_t sw[kMaxW], tw[kMaxW];
+    uint32_t tc = 0;
+#pragma unroll
+    for (int i = 0; i < kMaxW; ++i) {
+        const bool in = i < wpl && w0 + i < nw;
+        const uint32_t ew = in && eq_mode != 0 ? eqw[w0 + i] : 0u;
+        sw[i] = (in ? selw[w0 + i] : 0u) | (eq_mode == 2 ? ew : 0u);
+        tw[i] = eq_mode == 1 ? ew : (in ? tiew[w0 + i] : 0u);
+        tc += (uint32_t)__popc(tw[i]);
+    }
+    const uint32_t tincl = warp_incl_scan(tc, lane);
+    int32_t budget = remaining - (int32_t)(tincl - tc);  // ties left for this lane, in id order
+    uint32_t ns = 0;
+#pragma unroll
+    for (int i = 0; i < kMaxW; ++i) {
+        for (uint32_t m = tw[i]; m != 0u && budget > 0; m &= m - 1u, --budget) sw[i] |= m & (0u - m);
+        ns += (uint32_t)__popc(sw[i]);
+    }
+    const uint32_t sincl = warp_incl_scan(ns, lane);
+    int32_t slot = (int32_t)(sincl - ns);
+#pragma unroll
+    for (int i = 0; i < kMaxW; ++i)
+        for (uint32_t m = sw[i]; m != 0u && slot < K; m &= m - 1u, ++slot)
+            orow[slot] = (w0 + i) * 32 + __ffs(m) - 1;
+    const int32_t total = (int32_t)__shfl_sync(0xffffffffu, sincl, 31);
+    for (int32_t s2 = (total < K ? total : K) + lane; s2 < K; s2 += 32) orow[s2] = -1;
+}
 
 // 8 consecutive scores of a row as keys (vector loads when aligned).
 template <typename T>
@@ -255,27 +422,25 @@ template <typename T> __device__ __forceinline__ float key_value(uint32_t k);
 template <> __device__ __forceinline__ float key_value<float>(uint32_t k) {
     return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
 }
-template <> __device__ __forceinline__ float key_value<__nv_bfloat16>(uint32_t k) {
-    const uint32_t u = (k & 0x8000u) ? (k & 0x7FFFu) : (~k & 0xFFFFu);
-    return __bfloat162float(__ushort_as_bfloat16((unsigned short)u));
-}
-template <> __device__ __forceinline__ float key_value<__half>(uint32_t k) {
-    const uint32_t u = (k & 0x8000u) ? (k & 0x7FFFu) : (~k & 0xFFFFu);
-    return __half2float(__ushort_as_half((unsigned short)u));
-}
 
 // Each warp owns a contiguous run of rows.  Neighbouring rows of pooled block
-// scores are nearly identical, so the previous row's threshold, lowered by
-// kMargin key steps, is a good lower bound for this row's.  The pass that
-// loads the row compares every score with that bound (as a float: the key
-// order is the float order, and a superset of candidates is harmless) and
-// compacts the ones at or above it, in index order, into a candidate buffer;
-// keys are computed for candidates only, and the exact selection runs on them.
-// When the bound misses (no previous row, fewer than K candidates, or more
-// than the buffer holds) the row is staged in shared memory and the full
-// radix select runs on it.  Results never depend on which path ran.
+// scores are nearly identical, so the previous row's threshold hi, lowered by an
+// adaptive margin to t0, bounds this row's from below.
+//   16-bit scores: the pass that loads the row compares packed pairs with t0 and
+//   with hi; keys above t0 other than hi go to lane-private slots, keys equal to
+//   hi only to a bitmap (rows whose threshold is shared by many entries, such as
+//   the exact zeros of early causal tokens, store none of them).  Counting the
+//   keys above hi (G) and equal to it (E) decides: G < K <= G+E means the
+//   threshold is hi again and nothing is left to select; otherwise a histogram
+//   over the stored keys finds it.  Winners and ties become bitmaps over block
+//   ids that an in-order sweep turns into the sorted output.
+//   fp32 scores: the loading pass compares floats with t0 and compacts the
+//   candidates in index order; a radix select and an in-order emit follow.
+// When the bound misses (no previous row, fewer than K entries above it, or
+// more than the slots hold) the row is staged in shared memory as keys and the
+// full radix select runs on it.  Results never depend on which path ran.
 template <typename T>
-__global__ void __launch_bounds__(kWarps * 32)
+__global__ void __launch_bounds__(kWarps * 32, sizeof(T) == 2 ? 7 : 1)  // 16-bit: 7 blocks, <= 72 registers
 topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_stride, int32_t K,
             bool vec_ok, int64_t rows_per_warp, int32_t *__restrict__ out) {
     using Key = typename KeyOf<T>::K;
@@ -301,13 +466,105 @@ topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_
     for (int64_t row = r0; row < r1; ++row) {
         const T *src = scores + row * row_stride;
         int32_t *orow = out + row * K;
-        uint32_t prefix;
-        int32_t remaining;
-        bool take_all;
+        // the selection sets these warp-uniformly; tau_prev (from prefix) decides which path
+        // the whole warp takes on the next row, and that path uses full-warp collectives
+        uint32_t prefix = 0;
+        int32_t remaining = K;
+        bool take_all = true;
         bool done = false;
-        if (tau_prev) {
-            const uint32_t t0 = tau_prev > kMinFinite<Key> + margin ? tau_prev - margin
-                                                                    : kMinFinite<Key>;
+        if constexpr (sizeof(Key) == 2) {
+            if (tau_prev) {
+                // 16-bit scores.  hi = the previous row's threshold key, t0 = hi - margin.
+                // One pass with packed compares: keys > hi and keys in [t0, hi) go to
+                // lane-private slots (slot j of lane l at l + 32*j); keys == hi only set
+                // bits in a bitmap over block ids, so a row with many ties at the
+                // threshold (exact zeros of early causal tokens) stores none of them.
+                const uint32_t hi = tau_prev;
+                const uint32_t t0 = hi > kMinFinite<T> + margin ? hi - margin : kMinFinite<T>;
+                const uint32_t tb = key_bits16(t0), hb = key_bits16(hi);
+                const uint32_t t2 = tb | (tb << 16), h2 = hb | (hb << 16);
+                const int32_t nw = NBp >> 5;
+                uint32_t *eqw = reinterpret_cast<uint32_t *>(keys);  // the staging area is free here
+                uint32_t *selw = eqw + nw;
+                uint32_t *tiew = selw + nw;
+                for (int32_t i = lane; i < 3 * nw; i += 32) eqw[i] = 0u;
+                __syncwarp();
+                uint32_t cnt = 0, ngt = 0, neq = 0;
+                constexpr int BATCH = 8;  // steps (256 scores each) whose loads are in flight together
+                for (int32_t b0 = 0; b0 < NBp; b0 += 256 * BATCH) {
+                    uint4 raw[BATCH];
+#pragma unroll
+                    for (int st = 0; st < BATCH; ++st) {
+                        const int32_t i0 = b0 + st * 256 + 8 * lane;
+                        if (vec_ok && i0 + 8 <= NB) raw[st] = __ldg(reinterpret_cast<const uint4 *>(src + i0));
+                        else raw[st] = load8_bits_slow<T>(src, i0, NB);
+                    }
+#pragma unroll
+                    for (int st = 0; st < BATCH; ++st) {
+                        const uint32_t w[4] = {raw[st].x, raw[st].y, raw[st].z, raw[st].w};
+                        const uint32_t a = __byte_perm(ge2<T>(w[0], t2), ge2<T>(w[1], t2), 0x6420);
+                        const uint32_t b = __byte_perm(ge2<T>(w[2], t2), ge2<T>(w[3], t2), 0x6420);
+                        if ((a | b) == 0u) continue;
+                        const int32_t i0 = b0 + st * 256 + 8 * lane;
+                        // one 0xFF/0x00 byte per score -> 8-bit masks (the products sum disjoint bits)
+                        const uint32_t ea = __byte_perm(eq2<T>(w[0], h2), eq2<T>(w[1], h2), 0x6420);
+                        const uint32_t eb = __byte_perm(eq2<T>(w[2], h2), eq2<T>(w[3], h2), 0x6420);
+                        const uint32_t eqm = (((ea & 0x08040201u) * 0x01010101u) >> 24) |
+                                             (((eb & 0x80402010u) * 0x01010101u) >> 24);
+                        const uint32_t sel = ((((a & 0x08040201u) * 0x01010101u) >> 24) |
+                                              (((b & 0x80402010u) * 0x01010101u) >> 24)) & ~eqm;
+                        if (eqm) {
+                            atomicOr(&eqw[i0 >> 5], eqm << (i0 & 31));
+                            neq += (uint32_t)__popc(eqm);
+                        }
+                        for (uint32_t m = sel; m != 0u; m &= m - 1u) {
+                            const int e = __ffs(m) - 1;
+                            const uint32_t ww = (e & 4) ? ((e & 2) ? w[3] : w[2]) : ((e & 2) ? w[1] : w[0]);
+                            const uint32_t k = key16_bits((e & 1) ? (ww >> 16) : (ww & 0xFFFFu));
+                            if (cnt < (uint32_t)kLaneCand) {
+                                ckey[lane + 32 * cnt] = (Key)k;
+                                cidx[lane + 32 * cnt] = (uint16_t)(i0 + e);
+                            }
+                            ++cnt;
+                            ngt += k > hi ? 1u : 0u;
+                        }
+                    }
+                }
+                const int32_t n_st = (int32_t)__reduce_add_sync(0xffffffffu, cnt);   // stored
+                const int32_t G = (int32_t)__reduce_add_sync(0xffffffffu, ngt);      // > hi
+                const int32_t E = (int32_t)__reduce_add_sync(0xffffffffu, neq);      // == hi
+                const bool ovf = __any_sync(0xffffffffu, cnt > (uint32_t)kLaneCand);
+                const bool under = G + E + (n_st - G) < K;  // the threshold lies below t0
+                if (ovf) margin = margin / 2 > kMarginMin ? margin / 2 : kMarginMin;
+                else if (n_st > kCandCap / 4) margin = margin - margin / 4 > kMarginMin ? margin - margin / 4 : kMarginMin;
+                else if (under && t0 > kMinFinite<T>) margin = margin * 2 < kMarginMax ? margin * 2 : kMarginMax;
+                __syncwarp();
+                if (!ovf && !under) {
+                    const uint32_t mine = cnt;
+                    // 0: the threshold rose above hi (keys == hi are not taken); 1: it is hi
+                    // (no selection needed); 2: it fell into [t0, hi) (every key == hi taken)
+                    const int eq_mode = G >= K ? 0 : (G + E >= K ? 1 : 2);
+                    if (eq_mode == 1) {
+                        prefix = hi;
+                        remaining = K - G;
+                        take_all = false;
+                    } else {
+                        select_stored<Key, PASSES>(ckey, mine, t0, eq_mode == 0 ? K : K - E, hist, lane,
+                                                   prefix, remaining, take_all);
+                    }
+                    for (uint32_t j = 0; j < mine; ++j) {
+                        const uint32_t k = ckey[lane + 32 * j], id = cidx[lane + 32 * j];
+                        if (take_all || k > prefix) atomicOr(&selw[id >> 5], 1u << (id & 31));
+                        else if (k == prefix) atomicOr(&tiew[id >> 5], 1u << (id & 31));
+                    }
+                    __syncwarp();
+                    emit_bitmap(selw, tiew, eqw, eq_mode, nw, K, remaining, lane, orow);
+                    done = true;
+                }
+            }
+        } else if (tau_prev) {
+            const uint32_t t0 = tau_prev > kMinFinite<T> + margin ? tau_prev - margin
+                                                                    : kMinFinite<T>;
             const float tf = key_value<T>(t0);  // scores >= tf are candidates (NaN never is)
             int32_t n = 0;
             constexpr int VT = 16 / (int)sizeof(T);
@@ -360,7 +617,7 @@ topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_
             __syncwarp();
             if (n > kCandCap) margin = margin / 2 > kMarginMin ? margin / 2 : kMarginMin;
             else if (n > kCandCap / 2) margin = margin - margin / 4 > kMarginMin ? margin - margin / 4 : kMarginMin;
-            else if (n < K && t0 > kMinFinite<Key>) margin = margin * 2 < kMarginMax ? margin * 2 : kMarginMax;
+            else if (n < K && t0 > kMinFinite<T>) margin = margin * 2 < kMarginMax ? margin * 2 : kMarginMax;
             if (n >= K && n <= kCandCap) {
                 const int32_t npad = (n + 255) & ~255;
                 for (int32_t i = n + lane; i < npad; i += 32) ckey[i] = Key(0);
@@ -407,7 +664,9 @@ int launch_topk(const void *scores, int64_t rows, int64_t NB, int64_t row_stride
     UNUM_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     // a few long runs of consecutive rows per warp, so most rows reuse a threshold
     const int64_t want = (rows + kWarps - 1) / kWarps;
-    const int64_t cap = (int64_t)unum::sm_count() * 6;  // one resident wave (~29 KB of shared memory a block)
+    int per_sm = 0;  // one resident wave
+    UNUM_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kWarps * 32, smem));
+    const int64_t cap = (int64_t)unum::sm_count() * (per_sm > 0 ? per_sm : 1);
     const int grid = (int)(want < cap ? want : cap);
     const int64_t nwarps = (int64_t)grid * kWarps;
     const int64_t rows_per_warp = (rows + nwarps - 1) / nwarps;
