@@ -78,6 +78,14 @@ __device__ __forceinline__ uint32_t warp_incl_scan(uint32_t x, int lane) {
     return x;
 }
 
+// key of a 16-bit score that is neither NaN nor -inf, from its bits, and back
+__device__ __forceinline__ uint32_t key16_bits(uint32_t u) {
+    return (u & 0x8000u) ? (~u & 0xFFFFu) : (u | 0x8000u);
+}
+__device__ __forceinline__ uint32_t key_bits16(uint32_t k) {
+    return (k & 0x8000u) ? (k & 0x7FFFu) : (~k & 0xFFFFu);
+}
+
 // 8 consecutive keys from shared memory (i0 a multiple of 8) with 16-byte loads.
 template <typename Key>
 __device__ __forceinline__ void load8(const Key *keys, int32_t i0, uint32_t (&k)[8]) {
@@ -97,10 +105,19 @@ __device__ __forceinline__ void load8(const Key *keys, int32_t i0, uint32_t (&k)
     }
 }
 
-// Shared memory of one warp: histogram, staged keys, candidate keys and ids.
+// Candidate keys (512 slots) or, on the 16-bit path, three bitmaps over block ids.
+template <typename Key>
+__host__ __device__ constexpr size_t cand_region_bytes(size_t nbp) {
+    return 512 * sizeof(Key) > 12 * nbp / 32 ? 512 * sizeof(Key) : 12 * nbp / 32;
+}
+
+// Shared memory of one warp: histogram, staged keys (16-bit path: the row's raw
+// bits), candidate keys or, on the 16-bit path, three bitmaps over block ids, and
+// candidate ids.
 template <typename Key>
 __host__ __device__ constexpr size_t warp_smem_bytes(int64_t NB) {
-    return 1024 + ((NB + 255) / 256 * 256) * sizeof(Key) + 512 * sizeof(Key) + 512 * 2;
+    const size_t nbp = (size_t)((NB + 255) / 256 * 256);
+    return 1024 + nbp * sizeof(Key) + cand_region_bytes<Key>(nbp) + 512 * 2;
 }
 
 // Histogram of the staged keys[0, n_pad) whose bits under pmask equal prefix, by
@@ -199,24 +216,32 @@ __device__ __forceinline__ void radix_select(const Key *keys, int32_t n_pad, int
         K, hist, lane, prefix, remaining, take_all);
 }
 
-// K-th largest among the lane-private candidate keys (slot j of lane l at
-// l + 32*j, `mine` slots this lane).  One histogram pass over keys offset from
-// `base`: bins 1..254 hold single keys, bin 0 everything <= base, bin 255
-// everything >= base + 255, so when the K-th largest lands in bins 1..254 it is
-// exact; otherwise the 8-bit radix select settles it.  Same outputs as
-// radix_select_with.
+// K-th largest over one row of 16-bit scores, from the candidates of the
+// loading pass: the stored ids (slot j of lane l at l + 32*j, `mine` slots this
+// lane; their bits in rowb) plus E keys equal to hi, which were only counted.
+// One histogram pass over keys offset from t0: bins 1..254 hold single keys
+// (hi - t0 <= 128 is one of them and receives E), bin 0 everything <= t0, bin 255
+// everything >= t0 + 255.  When the K-th largest lands in bins 1..254 it is
+// exact; otherwise the 8-bit radix select over the stored keys settles it (the
+// keys == hi then lie on one side of the threshold: taken if it is below, so the
+// radix looks for the (K-E)-th largest, ignored if above).  Outputs as
+// radix_select_with over stored and equal keys together, where take_all covers
+// the stored keys only, plus eq_mode for the keys == hi: 0 not taken, 1 they are
+// the threshold's ties, 2 all taken.
 template <typename Key, int PASSES>
-__device__ __forceinline__ void select_stored(const Key *ckey, uint32_t mine, uint32_t base, int32_t K,
-                                              uint32_t *hist, int lane, uint32_t &prefix,
-                                              int32_t &remaining, bool &take_all) {
+__device__ __forceinline__ void select_row16(const uint16_t *rowb, const uint16_t *cidx, uint32_t mine,
+                                             uint32_t t0, uint32_t hi, int32_t E, int32_t K, uint32_t *hist,
+                                             int lane, uint32_t &prefix, int32_t &remaining, bool &take_all,
+                                             int &eq_mode) {
     reinterpret_cast<uint4 *>(hist)[2 * lane] = make_uint4(0u, 0u, 0u, 0u);
     reinterpret_cast<uint4 *>(hist)[2 * lane + 1] = make_uint4(0u, 0u, 0u, 0u);
     __syncwarp();
     for (uint32_t j = 0; j < mine; ++j) {
-        const uint32_t k = ckey[lane + 32 * j];
-        const uint32_t d = k <= base ? 0u : (k - base < 255u ? k - base : 255u);
+        const uint32_t k = key16_bits(rowb[cidx[lane + 32 * j]]);
+        const uint32_t d = k <= t0 ? 0u : (k - t0 < 255u ? k - t0 : 255u);
         atomicAdd(&hist[d], 1u);
     }
+    if (lane == 0 && E > 0) atomicAdd(&hist[hi - t0], (uint32_t)E);
     __syncwarp();
     uint32_t c[8];
     uint32_t sum = 0;
@@ -232,6 +257,7 @@ __device__ __forceinline__ void select_stored(const Key *ckey, uint32_t mine, ui
         prefix = 0;
         remaining = K;
         take_all = true;
+        eq_mode = 2;
         return;
     }
     const uint32_t excl = incl - sum;
@@ -253,19 +279,21 @@ __device__ __forceinline__ void select_stored(const Key *ckey, uint32_t mine, ui
     digit = __shfl_sync(0xffffffffu, digit, owner);
     above = __shfl_sync(0xffffffffu, above, owner);
     if (digit != 0u && digit != 255u) {
-        prefix = base + digit;
+        prefix = t0 + digit;
         remaining = K - (int32_t)above;
         take_all = false;
+        eq_mode = prefix > hi ? 0 : (prefix == hi ? 1 : 2);
         return;
     }
+    eq_mode = digit == 255u ? 0 : 2;
     radix_select_with<Key, PASSES>(
         [&](uint32_t pmask, uint32_t pre, int shift) {
             for (uint32_t j = 0; j < mine; ++j) {
-                const uint32_t k = ckey[lane + 32 * j];
+                const uint32_t k = key16_bits(rowb[cidx[lane + 32 * j]]);
                 if ((k & pmask) == pre) atomicAdd(&hist[(k >> shift) & 255u], 1u);
             }
         },
-        K, hist, lane, prefix, remaining, take_all);
+        digit == 255u ? K : K - E, hist, lane, prefix, remaining, take_all);
 }
 
 // Write the selected entries of keys[0, n) in index order to orow[0, K), then
@@ -336,13 +364,6 @@ template <typename T> constexpr uint32_t kNegInf16 = 0xFF80u;
 template <> constexpr uint32_t kNegInf16<__half> = 0xFC00u;
 template <typename T> __device__ __forceinline__ uint32_t bits16(T v) {
     return (uint32_t)(*reinterpret_cast<const uint16_t *>(&v));
-}
-// key of a 16-bit score that is neither NaN nor -inf, from its bits, and back
-__device__ __forceinline__ uint32_t key16_bits(uint32_t u) {
-    return (u & 0x8000u) ? (~u & 0xFFFFu) : (u | 0x8000u);
-}
-__device__ __forceinline__ uint32_t key_bits16(uint32_t k) {
-    return (k & 0x8000u) ? (k & 0x7FFFu) : (~k & 0xFFFFu);
 }
 
 // 8 scores from i0 as packed bits, -inf past the row end (unaligned rows, row tail);
@@ -452,7 +473,8 @@ topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_
     uint32_t *hist = reinterpret_cast<uint32_t *>(wbase);
     Key *keys = reinterpret_cast<Key *>(wbase + 1024);
     Key *ckey = keys + NBp;
-    uint16_t *cidx = reinterpret_cast<uint16_t *>(ckey + kCandCap);
+    uint16_t *cidx = reinterpret_cast<uint16_t *>(reinterpret_cast<uint8_t *>(ckey) +
+                                                  cand_region_bytes<Key>((size_t)NBp));
     const int64_t gw = (int64_t)blockIdx.x * kWarps + warp;
     const int64_t r0 = gw * rows_per_warp;
     const int64_t r1 = r0 + rows_per_warp < rows ? r0 + rows_per_warp : rows;
@@ -462,7 +484,8 @@ topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_
     // buffer, doubled when they were fewer than K
     uint32_t margin = kMargin<Key>;
     constexpr uint32_t kMarginMin = sizeof(Key) == 2 ? 1u : (1u << 16);
-    constexpr uint32_t kMarginMax = sizeof(Key) == 2 ? 1024u : (1024u << 16);
+    // 16-bit keys: at most 128 steps, so hi stays inside the exact bins of select_row16
+    constexpr uint32_t kMarginMax = sizeof(Key) == 2 ? 128u : (1024u << 16);
     for (int64_t row = r0; row < r1; ++row) {
         const T *src = scores + row * row_stride;
         int32_t *orow = out + row * K;
@@ -473,9 +496,11 @@ topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_
         bool take_all = true;
         bool done = false;
         if constexpr (sizeof(Key) == 2) {
-            if (tau_prev) {
+            // a row whose threshold fell below the bound gets one more pass with a 4x wider margin
+            for (int attempt = 0; attempt < 2 && tau_prev != 0u && !done; ++attempt) {
                 // 16-bit scores.  hi = the previous row's threshold key, t0 = hi - margin.
-                // One pass with packed compares: keys > hi and keys in [t0, hi) go to
+                // One pass stages the row's bits in shared memory and compares packed
+                // pairs with t0 and hi: ids of keys above t0 other than hi go to
                 // lane-private slots (slot j of lane l at l + 32*j); keys == hi only set
                 // bits in a bitmap over block ids, so a row with many ties at the
                 // threshold (exact zeros of early causal tokens) stores none of them.
@@ -484,12 +509,13 @@ topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_
                 const uint32_t tb = key_bits16(t0), hb = key_bits16(hi);
                 const uint32_t t2 = tb | (tb << 16), h2 = hb | (hb << 16);
                 const int32_t nw = NBp >> 5;
-                uint32_t *eqw = reinterpret_cast<uint32_t *>(keys);  // the staging area is free here
+                uint32_t *eqw = reinterpret_cast<uint32_t *>(ckey);
                 uint32_t *selw = eqw + nw;
                 uint32_t *tiew = selw + nw;
+                uint16_t *rowb = reinterpret_cast<uint16_t *>(keys);
                 for (int32_t i = lane; i < 3 * nw; i += 32) eqw[i] = 0u;
                 __syncwarp();
-                uint32_t cnt = 0, ngt = 0, neq = 0;
+                uint32_t cnt = 0, neq = 0;
                 constexpr int BATCH = 8;  // steps (256 scores each) whose loads are in flight together
                 for (int32_t b0 = 0; b0 < NBp; b0 += 256 * BATCH) {
                     uint4 raw[BATCH];
@@ -501,59 +527,43 @@ topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_
                     }
 #pragma unroll
                     for (int st = 0; st < BATCH; ++st) {
+                        const int32_t i0 = b0 + st * 256 + 8 * lane;
+                        if (b0 + st * 256 < NBp) *reinterpret_cast<uint4 *>(rowb + i0) = raw[st];
                         const uint32_t w[4] = {raw[st].x, raw[st].y, raw[st].z, raw[st].w};
                         const uint32_t a = __byte_perm(ge2<T>(w[0], t2), ge2<T>(w[1], t2), 0x6420);
                         const uint32_t b = __byte_perm(ge2<T>(w[2], t2), ge2<T>(w[3], t2), 0x6420);
                         if ((a | b) == 0u) continue;
-                        const int32_t i0 = b0 + st * 256 + 8 * lane;
                         // one 0xFF/0x00 byte per score -> 8-bit masks (the products sum disjoint bits)
                         const uint32_t ea = __byte_perm(eq2<T>(w[0], h2), eq2<T>(w[1], h2), 0x6420);
                         const uint32_t eb = __byte_perm(eq2<T>(w[2], h2), eq2<T>(w[3], h2), 0x6420);
                         const uint32_t eqm = (((ea & 0x08040201u) * 0x01010101u) >> 24) |
                                              (((eb & 0x80402010u) * 0x01010101u) >> 24);
-                        const uint32_t sel = ((((a & 0x08040201u) * 0x01010101u) >> 24) |
-                                              (((b & 0x80402010u) * 0x01010101u) >> 24)) & ~eqm;
+                        uint32_t sel = ((((a & 0x08040201u) * 0x01010101u) >> 24) |
+                                        (((b & 0x80402010u) * 0x01010101u) >> 24)) & ~eqm;
                         if (eqm) {
                             atomicOr(&eqw[i0 >> 5], eqm << (i0 & 31));
                             neq += (uint32_t)__popc(eqm);
                         }
-                        for (uint32_t m = sel; m != 0u; m &= m - 1u) {
-                            const int e = __ffs(m) - 1;
-                            const uint32_t ww = (e & 4) ? ((e & 2) ? w[3] : w[2]) : ((e & 2) ? w[1] : w[0]);
-                            const uint32_t k = key16_bits((e & 1) ? (ww >> 16) : (ww & 0xFFFFu));
-                            if (cnt < (uint32_t)kLaneCand) {
-                                ckey[lane + 32 * cnt] = (Key)k;
-                                cidx[lane + 32 * cnt] = (uint16_t)(i0 + e);
-                            }
-                            ++cnt;
-                            ngt += k > hi ? 1u : 0u;
-                        }
+                        for (; sel != 0u; sel &= sel - 1u, ++cnt)
+                            if (cnt < (uint32_t)kLaneCand) cidx[lane + 32 * cnt] = (uint16_t)(i0 + __ffs(sel) - 1);
                     }
                 }
-                const int32_t n_st = (int32_t)__reduce_add_sync(0xffffffffu, cnt);   // stored
-                const int32_t G = (int32_t)__reduce_add_sync(0xffffffffu, ngt);      // > hi
-                const int32_t E = (int32_t)__reduce_add_sync(0xffffffffu, neq);      // == hi
+                const int32_t n_st = (int32_t)__reduce_add_sync(0xffffffffu, cnt);  // stored
+                const int32_t E = (int32_t)__reduce_add_sync(0xffffffffu, neq);     // == hi
                 const bool ovf = __any_sync(0xffffffffu, cnt > (uint32_t)kLaneCand);
-                const bool under = G + E + (n_st - G) < K;  // the threshold lies below t0
+                const bool under = n_st + E < K;  // the threshold lies below t0
                 if (ovf) margin = margin / 2 > kMarginMin ? margin / 2 : kMarginMin;
                 else if (n_st > kCandCap / 4) margin = margin - margin / 4 > kMarginMin ? margin - margin / 4 : kMarginMin;
                 else if (under && t0 > kMinFinite<T>) margin = margin * 2 < kMarginMax ? margin * 2 : kMarginMax;
                 __syncwarp();
                 if (!ovf && !under) {
                     const uint32_t mine = cnt;
-                    // 0: the threshold rose above hi (keys == hi are not taken); 1: it is hi
-                    // (no selection needed); 2: it fell into [t0, hi) (every key == hi taken)
-                    const int eq_mode = G >= K ? 0 : (G + E >= K ? 1 : 2);
-                    if (eq_mode == 1) {
-                        prefix = hi;
-                        remaining = K - G;
-                        take_all = false;
-                    } else {
-                        select_stored<Key, PASSES>(ckey, mine, t0, eq_mode == 0 ? K : K - E, hist, lane,
-                                                   prefix, remaining, take_all);
-                    }
+                    int eq_mode;  // keys == hi: below the threshold (0), its ties (1) or all taken (2)
+                    select_row16<Key, PASSES>(rowb, cidx, mine, t0, hi, E, K, hist, lane, prefix, remaining,
+                                              take_all, eq_mode);
                     for (uint32_t j = 0; j < mine; ++j) {
-                        const uint32_t k = ckey[lane + 32 * j], id = cidx[lane + 32 * j];
+                        const uint32_t id = cidx[lane + 32 * j];
+                        const uint32_t k = key16_bits(rowb[id]);
                         if (take_all || k > prefix) atomicOr(&selw[id >> 5], 1u << (id & 31));
                         else if (k == prefix) atomicOr(&tiew[id >> 5], 1u << (id & 31));
                     }
@@ -561,6 +571,9 @@ topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_
                     emit_bitmap(selw, tiew, eqw, eq_mode, nw, K, remaining, lane, orow);
                     done = true;
                 }
+                // overflow, or no finite bound left to lower: the staged radix select below
+                if (!under || t0 <= kMinFinite<T>) break;
+                margin = margin * 2 < kMarginMax ? margin * 2 : kMarginMax;  // x4 with the update above
             }
         } else if (tau_prev) {
             const uint32_t t0 = tau_prev > kMinFinite<T> + margin ? tau_prev - margin
