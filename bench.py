@@ -12,9 +12,12 @@ calls are also timed, as context (`kernels_api_path`).  Inputs and
 outputs (q 1.07 GB, scores 4.3 GB, slots 4.3 GB) are far larger than the
 126 MB L2, so no explicit flush is needed between steps.
 
-Multi-GPU (torchrun, one process per GPU): every rank runs its own 128k
-sequence (independent units, no collective on the data path); the step time
-is the max over ranks, value = N * 131072 tokens / step time (weak scaling).
+Multi-GPU (torchrun, one process per GPU), config 3's sharding: the one
+128k sequence is split into kv head x query range shards (ranges of equal
+stage-1 plus per-token work); each rank computes its shard with no exchange,
+then the top-k ids are all-gathered (NCCL) inside the step.  The step time is
+the max over ranks, value = 131072 tokens / step time (strong scaling).
+--scaling weak gives every rank its own sequence instead.
 
 --impl reference times the reference's CPU path on this host: the C
 restatement of the reference's torch/Triton semantics (oracle/, "port"),
@@ -51,22 +54,36 @@ def visible_counts(L=None, k_len=None):
     return np.clip(off, 0, k_len)
 
 
-def stage1_flops():
-    """Algorithmic work of stage 1: one QK^T pass over the visible pairs."""
-    return float(2 * D * HQ * visible_counts().sum())
+def stage1_flops(t_begin=0, t_end=None):
+    """Algorithmic work of stage 1 over query rows [t_begin, t_end), all q heads: one
+    QK^T pass over the visible pairs."""
+    return float(2 * D * HQ * visible_counts()[t_begin:t_end].sum())
 
 
-def algorithmic_bytes():
-    """Per-kernel algorithmic HBM bytes of one step (bf16 scores, int32 ids)."""
+def algorithmic_bytes(T=None, nh=HK):
+    """Per-kernel algorithmic HBM bytes of one step over T query rows of nh kv heads
+    (bf16 scores, int32 ids)."""
     W = (NKC + 127) // 128 * 128
     NB = (L_SEQ + 63) // 64
-    T = L_SEQ
+    T = L_SEQ if T is None else T
     return {
-        "pool": HK * T * W * 2 + HK * T * NB * 2,
-        "topk": HK * T * NB * 2 + HK * T * TOPK * 4,
-        "get_block_table": T * HK * TOPK * 64 * 4 + HK * T * TOPK * 4 + 8 * T + 4 * L_SEQ,
-        "stage1_out": HK * T * W * 2,
+        "pool": nh * T * W * 2 + nh * T * NB * 2,
+        "topk": nh * T * NB * 2 + nh * T * TOPK * 4,
+        "get_block_table": T * nh * TOPK * 64 * 4 + nh * T * TOPK * 4 + 8 * T + 4 * T,
+        "stage1_out": nh * T * W * 2,
     }
+
+
+MUFU_EX2_PER_CLK_SM = 16  # ex2.approx results per clock per SM, measured on this B200 pool
+
+
+def mufu_roofline(flops, ms, clocks):
+    """Stage 1's second ceiling: its softmax takes two exponentials per visible
+    (query head, key) pair (one per pass), flops / D of them, on the MUFU unit."""
+    exps = flops / D
+    mhz = clocks.get("sm_mhz") or 1965.0
+    floor_ms = exps / (MUFU_EX2_PER_CLK_SM * 148 * mhz * 1e6) * 1e3
+    return {"exp2_per_launch": exps, "sm_mhz": mhz, "floor_ms": floor_ms, "frac": floor_ms / ms}
 
 
 def workload_name():
@@ -202,16 +219,39 @@ def make_inputs(seed, device):
 
 
 # ------------------------------------------------------------------ our arm
+# Per-token work of pooling, top-k and get_block_table, in units of one visible
+# compressed key of stage 1 (both per kv head), from the kernel times at 128k:
+# stage 1 ~1.0e-11 s per key, top-k + block table ~5.6e-9 s per (token, head).
+TOKEN_COST = 560.0
+
+
+def shard_of(world, rank, strong):
+    """(first kv head, kv heads, t_begin, t_end) this rank computes.
+
+    Strong scaling (config 3's sharding): with an even rank count each rank owns one
+    kv head and one of world/2 query ranges of equal work; otherwise both heads and
+    one of `world` ranges.  Weak scaling: the whole sequence (every rank its own)."""
+    from unum_ops_b200.sharding import plan_query_ranges
+
+    if world == 1 or not strong:
+        return 0, HK, 0, L_SEQ
+    if world % HK == 0:
+        g, nh, n_r, r = rank % HK, 1, world // HK, rank // HK
+    else:
+        g, nh, n_r, r = 0, HK, world, rank
+    a, b = plan_query_ranges(L_SEQ, NKC, n_r, token_cost=TOKEN_COST)[r]
+    return g, nh, a, b
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
 
     import unum_ops_b200
-    from unum_ops_b200 import block_select_streamed
+    from unum_ops_b200 import block_select_streamed, get_block_table_shard
     from unum_ops_b200.block_select import stage1_pooled
-    from unum_ops_b200.infllm_v2 import (infllmv2_attn_stage1, max_pooling_1d_varlen,
+    from unum_ops_b200.infllm_v2 import (_workspace, infllmv2_attn_stage1, max_pooling_1d_varlen,
                                          stage1_status)
-    from unum_ops_b200.sparse_kernel_extension import get_block_table_ref_torch
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -221,30 +261,65 @@ def run_ours(args):
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
     unum_ops_b200.load()
+    L = unum_ops_b200.load()
+    strong = args.scaling == "strong"
+    g0, nh, ta, tb_ = shard_of(world, rank, strong)
+    nrows = tb_ - ta
+    G = HQ // HK
 
-    host = make_inputs(1234 + 3 + rank, dev)
+    # strong scaling: every rank holds the same global input (one seed) and computes
+    # its shard; weak scaling: every rank its own sequence
+    host = make_inputs(1234 + 3 + (0 if strong else rank), dev)
     d = {k: v.to(dev) for k, v in host.items()}
+    q_s = d["q"][:, g0 * G:(g0 + nh) * G]   # this rank's query heads (a strided view)
+    k_s = d["k"][:, g0:g0 + nh]
     stream = torch.cuda.current_stream(dev)
     W = (NKC + 127) // 128 * 128
+    NB = (L_SEQ + 63) // 64
     zeros_cache = torch.zeros(1, dtype=torch.int32, device=dev)
+    scores = torch.empty(nh, L_SEQ, W, dtype=torch.bfloat16, device=dev)
+    pooled = torch.empty(nh, L_SEQ, NB, dtype=torch.bfloat16, device=dev)
+    idx = torch.empty(nh, nrows, TOPK, dtype=torch.int32, device=dev)
+    slots = torch.empty(nrows, nh, TOPK * 64, dtype=torch.int32, device=dev)
+    ws = _workspace(dev, int(L.unum_stage1_workspace_size(1)))
+    # topk_idx of all ranks in one place: padded to the longest range
+    ranges = [shard_of(world, r, strong) for r in range(world)]
+    pad_rows = max(r[3] - r[2] for r in ranges)
+    gather_src = torch.zeros(nh, pad_rows, TOPK, dtype=torch.int32, device=dev)
+    gather_dst = torch.empty(world, nh, pad_rows, TOPK, dtype=torch.int32, device=dev)
 
     def step(ev=None):
-        """One block-selection pass as block_select runs it: stage 1 with the pooling
-        fused in, top-k, get_block_table."""
+        """One block-selection pass over this rank's shard: stage 1 with the pooling
+        fused in (token window [ta, tb_) of kv heads g0..g0+nh-1), top-k, get_block_table;
+        with several ranks, the top-k ids are then gathered on every rank."""
         if ev is not None:
             ev[0].record(stream)
-        scores, pooled = stage1_pooled(d["q"], d["k"], d["cu_q"], d["cu_k"], NKC, L_SEQ,
-                                       LOCAL_BLOCKS, INIT_BLOCKS, causal=True)
+        unum_ops_b200._lib.check(L.unum_infllmv2_attn_stage1_window(
+            q_s.data_ptr(), L_SEQ, nh * G, D, q_s.stride(0), q_s.stride(1), k_s.data_ptr(), NKC, nh,
+            k_s.stride(0), k_s.stride(1), d["cu_q"].data_ptr(), d["cu_k"].data_ptr(), 1, D ** -0.5, 1,
+            scores.data_ptr(), W, pooled.data_ptr(), NB, INIT_BLOCKS, LOCAL_BLOCKS, ta, tb_,
+            ws.data_ptr(), ws.numel(), stream.cuda_stream))
         if ev is not None:
             ev[1].record(stream)
+        if nrows == L_SEQ:  # every row: one launch over the heads' rows together
+            unum_ops_b200._lib.check(L.unum_topk_blocks(
+                pooled.data_ptr(), 1, nh * nrows, NB, NB, TOPK, idx.data_ptr(), stream.cuda_stream))
+        else:
+            for h in range(nh):
+                unum_ops_b200._lib.check(L.unum_topk_blocks(
+                    pooled[h, ta:tb_].data_ptr(), 1, nrows, NB, NB, TOPK, idx[h].data_ptr(),
+                    stream.cuda_stream))
+        if ev is not None:
             ev[2].record(stream)
-        idx = unum_ops_b200.topk_blocks(pooled, TOPK)
+        get_block_table_shard(idx, d["table"], d["tb"][ta:tb_], d["pos"][ta:tb_], d["seqlen"],
+                              head_offset=g0, out=slots)
         if ev is not None:
             ev[3].record(stream)
-        slots = get_block_table_ref_torch(idx, d["table"], d["tb"], d["pos"], d["seqlen"])
+        if world > 1:
+            gather_src[:, :nrows].copy_(idx)
+            dist.all_gather_into_tensor(gather_dst, gather_src)
         if ev is not None:
             ev[4].record(stream)
-        return scores, pooled, idx, slots
 
     def barrier():
         if world > 1:
@@ -253,11 +328,10 @@ def run_ours(args):
 
     clk = ClockSampler(local).start()
     for _ in range(args.warmup):
-        out = step()
+        step()
     barrier()
     if stage1_status(dev) != 0:
         raise RuntimeError("stage-1 kernel reported a timeout")
-    del out
 
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
     t_start = torch.cuda.Event(enable_timing=True)
@@ -266,54 +340,59 @@ def run_ours(args):
     wall0 = time.time()
     t_start.record(stream)
     for i in range(args.steps):
-        out = step(evs[i])
+        step(evs[i])
     t_end.record(stream)
     barrier()
     wall1 = time.time()
     clk.stop()
     total_ms = t_start.elapsed_time(t_end)
-    per = {"stage1": [], "topk": [], "get_block_table": []}
+    per = {"stage1": [], "topk": [], "get_block_table": [], "gather": []}
     for e in evs:
         per["stage1"].append(e[0].elapsed_time(e[1]))
-        per["topk"].append(e[2].elapsed_time(e[3]))
-        per["get_block_table"].append(e[3].elapsed_time(e[4]))
-    # context: the four separate reference-API calls (stage 1, pooling, top-k, block table)
-    api = {"stage1": [], "pool": []}
-    for _ in range(3):
-        a0, a1, a2 = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-        a0.record(stream)
-        sc = infllmv2_attn_stage1(d["q"], d["k"], None, d["cu_q"], d["cu_k"], max_seqlen_k=NKC,
-                                  causal=True)
-        a1.record(stream)
-        max_pooling_1d_varlen(sc, d["cu_q"], d["cu_k"], zeros_cache, 16 * W, L_SEQ, LOCAL_BLOCKS,
-                              INIT_BLOCKS)
-        a2.record(stream)
-        torch.cuda.synchronize(dev)
-        api["stage1"].append(a0.elapsed_time(a1))
-        api["pool"].append(a1.elapsed_time(a2))
-        del sc
+        per["topk"].append(e[1].elapsed_time(e[2]))
+        per["get_block_table"].append(e[2].elapsed_time(e[3]))
+        per["gather"].append(e[3].elapsed_time(e[4]))
     ms_step = total_ms / args.steps
     if world > 1:
         t = torch.tensor([ms_step], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_step = float(t.item())
-    del out
+    api = None
+    if world == 1:
+        # context: the separate reference-API calls for stage 1 and pooling
+        api = {"stage1": [], "pool": []}
+        for _ in range(3):
+            a0, a1, a2 = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            a0.record(stream)
+            sc = infllmv2_attn_stage1(d["q"], d["k"], None, d["cu_q"], d["cu_k"], max_seqlen_k=NKC,
+                                      causal=True)
+            a1.record(stream)
+            max_pooling_1d_varlen(sc, d["cu_q"], d["cu_k"], zeros_cache, 16 * W, L_SEQ, LOCAL_BLOCKS,
+                                  INIT_BLOCKS)
+            a2.record(stream)
+            torch.cuda.synchronize(dev)
+            api["stage1"].append(a0.elapsed_time(a1))
+            api["pool"].append(a1.elapsed_time(a2))
+            del sc
+    del scores, pooled, slots
 
-    # ---- end to end through the public API with host buffers (pinned), copies timed
-    pin = {k: v.pin_memory() for k, v in host.items()}
-    res_host = torch.empty(HK, L_SEQ, TOPK, dtype=torch.int32).pin_memory()
+    # ---- end to end through the public API with host buffers (pinned), copies timed:
+    # this rank's query rows of its kv heads stream in, its top-k ids go back to the host
+    q_pin = host["q"][ta:tb_, g0 * G:(g0 + nh) * G].contiguous().pin_memory()
+    pin = {k: v.pin_memory() for k, v in host.items() if k != "q"}
+    res_host = torch.empty(nh, nrows, TOPK, dtype=torch.int32).pin_memory()
 
     def e2e_step():
         """Through the public streamed API: host-resident queries copied in chunk by chunk
         while the previous chunk computes; the top-k ids come back to pinned host memory."""
-        kk = pin["k"].to(dev, non_blocking=True)
+        kk = pin["k"][:, g0:g0 + nh].to(dev, non_blocking=True)
         small = {n: pin[n].to(dev, non_blocking=True) for n in ("cu_q", "cu_k", "table", "tb", "pos",
                                                                  "seqlen")}
-        _, _, idx, slots = block_select_streamed(
-            pin["q"], kk, small["cu_q"], small["cu_k"], NKC, small["table"], small["tb"],
+        block_select_streamed(
+            q_pin, kk, small["cu_q"], small["cu_k"], NKC, small["table"], small["tb"],
             small["pos"], small["seqlen"], max_context_len=L_SEQ, init_blocks=INIT_BLOCKS,
-            local_blocks=LOCAL_BLOCKS, topk=TOPK, chunk_tokens=16384, result_host=res_host)
-        return slots
+            local_blocks=LOCAL_BLOCKS, topk=TOPK, chunk_tokens=16384, result_host=res_host,
+            t_begin=ta, head_offset=g0)
 
     e2e_step()
     barrier()
@@ -329,14 +408,20 @@ def run_ours(args):
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    h2d = sum(v.numel() * v.element_size() for v in pin.values())
+    h2d = q_pin.numel() * 2 + pin["k"][:, g0:g0 + nh].numel() * 2 + sum(
+        pin[n].numel() * pin[n].element_size() for n in ("cu_q", "cu_k", "table", "tb", "pos", "seqlen"))
     d2h = res_host.numel() * 4
+    if world > 1:  # whole-job bytes: every rank's copies
+        t = torch.tensor([h2d, d2h], dtype=torch.float64, device=dev)
+        dist.all_reduce(t)
+        h2d, d2h = int(t[0].item()), int(t[1].item())
 
     if rank == 0:
+        clocks = clk.summary(wall0, wall1)
         hbm, tf_burst, tf_sus, src = load_peaks()
         mean = {k: statistics.mean(v) for k, v in per.items()}
-        flops = stage1_flops()
-        ab = algorithmic_bytes()
+        flops = stage1_flops(ta, tb_) * nh / HK
+        ab = algorithmic_bytes(nrows, nh)
         traffic = load_traffic()
         s1_tf = flops / (mean["stage1"] * 1e-3) / 1e12
         kernels = {
@@ -347,49 +432,60 @@ def run_ours(args):
         for kname in ("topk", "get_block_table"):
             gbs = ab[kname] / (mean[kname] * 1e-3) / 1e9
             kernels[kname] = {"ms": mean[kname], "gbs": gbs, "frac": gbs / hbm, "bound": "hbm"}
-        am = {k2: statistics.mean(v) for k2, v in api.items()}
-        pool_gbs = ab["pool"] / (am["pool"] * 1e-3) / 1e9
-        kernels_api = {"stage1": {"ms": am["stage1"]},
-                       "pool": {"ms": am["pool"], "gbs": pool_gbs, "frac": pool_gbs / hbm,
-                                "bound": "hbm"},
-                       "note": "separate max_pooling_1d_varlen call; the step fuses it into stage1"}
+        if world > 1:
+            kernels["topk_idx_all_gather"] = {"ms": mean["gather"], "bytes": gather_dst.numel() * 4}
         cpu = None
-        if args.cpu_sample > 0:
+        if args.cpu_sample > 0 and world == 1:
             hf = {k: v.numpy() for k, v in host.items() if k not in ("q", "k")}
             hf["q"] = host["q"].float().numpy()
             hf["k"] = host["k"].float().numpy()
             cpu = cpu_baseline(args, sample_tokens=args.cpu_sample, host=hf)
+        if strong and world > 1:
+            par = (f"{world} ranks: kv head x query range ({HK} x {world // HK})" if world % HK == 0
+                   else f"{world} query ranges") + ", ranges of equal stage-1 + per-token work"
+        else:
+            par = f"dp{world} (one sequence per GPU)"
+        tokens = L_SEQ if strong else world * L_SEQ
         line = {
             "metric": METRIC,
-            "value": world * L_SEQ / (ms_step * 1e-3),
+            "value": tokens / (ms_step * 1e-3),
             "unit": "tokens/s",
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": ms_step,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if strong else "weak",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) q/k_cmp, random-permutation block table)",
             "config": {"workload": workload_name(),
-                       "tokens_per_gpu": L_SEQ, "parallelism": f"dp{world} (one sequence per GPU)",
+                       "tokens_total": tokens, "parallelism": par,
+                       "rank0_shard": {"kv_heads": [g0, g0 + nh], "tokens": [ta, tb_]},
                        "l2": "inputs larger than L2 (q 1.07 GB, scores 4.3 GB, slots 4.3 GB)"},
             "roofline": {"bound": "tensor", "kernel": "stage1", "achieved": s1_tf,
                          "peak": tf_sus, "unit": "TFLOP/s", "frac": s1_tf / tf_sus,
                          "peak_source": f"{src} bf16_tflops_sustained",
-                         "algorithmic": "2*D*Hq*sum_t visible(t) = %.4g flop per launch" % flops,
-                         "traffic": traffic.get("stage1")},
+                         "algorithmic": "2*D*G*sum_t visible(t) over rank 0's shard = %.4g flop "
+                                        "per launch" % flops,
+                         "traffic": traffic.get("stage1") if world == 1 else None,
+                         "mufu": mufu_roofline(flops, mean["stage1"], clocks)},
             "kernels": kernels,
-            "e2e": {"value": world * L_SEQ / (e2e_ms * 1e-3), "unit": "tokens/s",
+            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-                    "result": "top-64 block ids int32 [2,131072,64] copied to host",
+                    "result": "top-64 block ids int32 of every rank's shard copied to host",
                     "api": "block_select_streamed (query chunks of 16384 tokens copied while the "
                            "previous chunk computes)"},
-            "kernels_api_path": kernels_api,
-            "gpu_launches": 4 * args.steps,
-            "clocks": clk.summary(wall0, wall1),
+            "gpu_launches": (2 + (1 if nrows == L_SEQ else nh)) * args.steps,
+            "clocks": clocks,
         }
+        if api is not None:
+            am = {k2: statistics.mean(v) for k2, v in api.items()}
+            pool_gbs = ab["pool"] / (am["pool"] * 1e-3) / 1e9
+            line["kernels_api_path"] = {
+                "stage1": {"ms": am["stage1"]},
+                "pool": {"ms": am["pool"], "gbs": pool_gbs, "frac": pool_gbs / hbm, "bound": "hbm"},
+                "note": "separate max_pooling_1d_varlen call; the step fuses it into stage1"}
         if cpu is not None:
             line["cpu_baseline"] = cpu
         emit(line)
@@ -400,13 +496,16 @@ def run_ours(args):
 
 # ------------------------------------------------------------------ decode batch (config 4)
 def run_decode(args):
-    """512 sequences x 1 query token, contexts U[4096, 65536], every rank
-    its own batch (weak scaling).  A step is block_select on the batch."""
+    """512 sequences x 1 query token, contexts U[4096, 65536].  A step is
+    block_select on the batch.  With N ranks the batch is split by longest-processing-time
+    packing of the sequences' compressed-key counts (strong scaling; --scaling weak gives
+    every rank its own batch) and the top-k ids are all-gathered inside the step."""
     import torch
     import torch.distributed as dist
 
     import unum_ops_b200
     from unum_ops_b200 import block_select
+    from unum_ops_b200.sharding import plan_sequences, sequence_cost
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -416,24 +515,47 @@ def run_decode(args):
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
     unum_ops_b200.load()
-    B = 512
-    rng = np.random.default_rng(4 + rank)
-    ctx = rng.integers(4096, 65537, size=B)
-    k_lens = (ctx - 32) // 16 + 1
-    g = torch.Generator(device=dev).manual_seed(4 + rank)
-    q = torch.randn(B, HQ, D, generator=g, device=dev).to(torch.bfloat16)
-    k = torch.randn(int(k_lens.sum()), HK, D, generator=g, device=dev).to(torch.bfloat16)
+    strong = args.scaling == "strong"
+    B_all = 512
+    seed = 4 + (0 if strong else rank)
+    rng = np.random.default_rng(seed)
+    ctx_all = rng.integers(4096, 65537, size=B_all)
+    k_lens_all = (ctx_all - 32) // 16 + 1
+    table_all = rng.integers(0, 1 << 20, size=(B_all, 1024)).astype(np.int32)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    q_all = torch.randn(B_all, HQ, D, generator=g, device=dev).to(torch.bfloat16)
+    k_all = torch.randn(int(k_lens_all.sum()), HK, D, generator=g, device=dev).to(torch.bfloat16)
+    if strong and world > 1:
+        plan = plan_sequences(sequence_cost([1] * B_all, k_lens_all), world)
+    else:
+        plan = [list(range(B_all))] * world
+    mine = np.array(plan[rank], np.int64)
+    B = len(mine)
+    starts = np.concatenate([[0], np.cumsum(k_lens_all)])
+    k_rows = np.concatenate([np.arange(starts[i], starts[i + 1]) for i in mine])
+    k_lens = k_lens_all[mine]
+    ctx = ctx_all[mine]
+    q = q_all[torch.from_numpy(mine).to(dev)].contiguous()
+    k = k_all[torch.from_numpy(k_rows).to(dev)].contiguous()
+    del q_all, k_all
     cu_q = torch.arange(B + 1, dtype=torch.int32, device=dev)
     cu_k = torch.from_numpy(np.concatenate([[0], np.cumsum(k_lens)]).astype(np.int32)).to(dev)
-    table = torch.from_numpy(rng.integers(0, 1 << 20, size=(B, 1024)).astype(np.int32)).to(dev)
+    table = torch.from_numpy(table_all[mine]).to(dev)
     tb = torch.arange(B, dtype=torch.int32, device=dev)
     pos = torch.from_numpy(ctx.astype(np.int32)).to(dev)
     cache = torch.from_numpy((ctx - 1).astype(np.int32)).to(dev)
     stream = torch.cuda.current_stream(dev)
+    pad = max(len(p) for p in plan)
+    gather_src = torch.zeros(HK, pad, TOPK, dtype=torch.int32, device=dev)
+    gather_dst = torch.empty(world, HK, pad, TOPK, dtype=torch.int32, device=dev)
 
     def step():
-        return block_select(q, k, cu_q, cu_k, int(k_lens.max()), table, tb, pos, pos,
-                            max_context_len=65536, cache_lens=cache)
+        out = block_select(q, k, cu_q, cu_k, int(k_lens.max()), table, tb, pos, pos,
+                           max_context_len=65536, cache_lens=cache)
+        if world > 1:
+            gather_src[:, :B].copy_(out[2])
+            dist.all_gather_into_tensor(gather_dst, gather_src)
+        return out
 
     for _ in range(args.warmup):
         step()
@@ -456,13 +578,17 @@ def run_decode(args):
     kbytes = int(k_lens.sum()) * HK * D * 2
     if rank == 0:
         hbm = load_peaks()[0]
+        seqs = B_all if strong else world * B_all
         emit({
             "metric": "decode block selection, sequences/s (512 x 1 query, contexts U[4096,65536])",
-            "value": world * B / (ms * 1e-3), "unit": "sequences/s", "n_gpus": world,
+            "value": seqs / (ms * 1e-3), "unit": "sequences/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded)", "config": {"workload": "C4 decode batch",
-                                                     "k_cmp_bytes": kbytes},
+            "higher_is_better": True, "scaling": "strong" if strong else "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+            "config": {"workload": "C4 decode batch",
+                       "parallelism": (f"{world} ranks, sequences by LPT on compressed-key counts"
+                                       if strong and world > 1 else f"dp{world}"),
+                       "rank0_sequences": B, "rank0_k_cmp_bytes": kbytes},
             "k_cmp_stream_gbs": kbytes / (ms * 1e-3) / 1e9,
             "k_cmp_stream_frac": kbytes / (ms * 1e-3) / 1e9 / hbm})
     if world > 1:
@@ -564,6 +690,9 @@ def main():
                     help="prefill: the 128k headline (config 3); decode: config 4")
     ap.add_argument("--seqlen", type=int, default=131072,
                     help="prefill length (default: the 128k headline workload)")
+    ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
+                    help="N>1: strong = one sequence sharded by kv head x query range "
+                         "(config 3); weak = every rank its own sequence")
     args = ap.parse_args()
     global L_SEQ, NKC
     L_SEQ = args.seqlen

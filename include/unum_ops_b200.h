@@ -74,6 +74,25 @@ int unum_get_block_table(const int32_t *topk_idx, int64_t H, int64_t T, int64_t 
                          int32_t head_group, int32_t *out, void *stream);
 
 /*
+ * get_block_table_shard — get_block_table for a shard of kv heads (and tokens),
+ * for a rank that owns heads [head_offset, head_offset + H) of a token range.
+ * No single reference function: the reference computes every head in one call.
+ *
+ *   topk_idx, token_to_bs, token_pos_in_bs: the shard's H heads and T tokens
+ *   out[t * out_token_stride + h*K*64 + k*64 + i] for the shard's (t, h), with
+ *       the value of get_block_table for head index head_offset + h;
+ *   out_token_stride >= H*K*64, a multiple of 4 (H*K*64 for a dense shard, or the
+ *       full model's Hk*K*64 with out pointing at head head_offset of token 0).
+ */
+int unum_get_block_table_shard(const int32_t *topk_idx, int64_t H, int64_t T, int64_t K,
+                               int64_t ts_h, int64_t ts_t, int64_t ts_k,
+                               const int32_t *block_table, int64_t B, int64_t L, int64_t bt_stride,
+                               const int32_t *token_to_bs, const int32_t *token_pos_in_bs,
+                               int pos_is_scalar, const int32_t *seqlen_q, int seqlen_is_scalar,
+                               int32_t head_group, int64_t head_offset, int64_t out_token_stride,
+                               int32_t *out, void *stream);
+
+/*
  * max_pooling_1d_varlen — compressed scores to 64-token-block scores.
  * Replaces max_pooling_1d_varlen_ref_triton (max_pooling_1d_varlen.py:127-183).
  *

@@ -383,3 +383,81 @@ def test_block_select_streamed_back_to_back(dev):
     torch.cuda.synchronize()
     for i, o in enumerate(outs):
         assert torch.equal(o, refs[i % 2]), i
+
+
+# ---------------------------------------------------------------- sharded rows
+def _c3_like(L, seed, dev):
+    nk = cases.compressed_len(L)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    q = torch.randn(L, 32, 128, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(nk, 2, 128, generator=g, device=dev).to(torch.bfloat16)
+    cu_q = torch.tensor([0, L], dtype=torch.int32, device=dev)
+    cu_k = torch.tensor([0, nk], dtype=torch.int32, device=dev)
+    table = torch.randperm(L, device=dev, dtype=torch.int64).to(torch.int32).reshape(1, L)
+    tb = torch.zeros(L, dtype=torch.int32, device=dev)
+    pos = torch.arange(1, L + 1, dtype=torch.int32, device=dev)
+    sl = torch.tensor([L], dtype=torch.int32, device=dev)
+    return q, k, cu_q, cu_k, nk, table, tb, pos, sl
+
+
+@pytest.mark.parametrize("n_ranges", [1, 3])
+def test_rows_shards_equal_full(n_ranges, dev):
+    """Every (kv head, query range) shard of one causal sequence reproduces the
+    unsharded path's rows bit for bit: scores, pooled scores, top-k ids, slots."""
+    from unum_ops_b200 import block_select, block_select_rows, sharding
+
+    L = 16384
+    q, k, cu_q, cu_k, nk, table, tb, pos, sl = _c3_like(L, 11, dev)
+    full = block_select(q, k, cu_q, cu_k, nk, table, tb, pos, sl, max_context_len=L)
+    for g in range(2):
+        qg, kg = q[:, 16 * g:16 * (g + 1)], k[:, g:g + 1]  # strided views of one kv group
+        for a, b in sharding.plan_query_ranges(L, nk, n_ranges, token_cost=600.0):
+            sc, po, idx, slots = block_select_rows(qg, kg, cu_q, cu_k, nk, table, tb, pos, sl,
+                                                   t_begin=a, t_end=b, max_context_len=L,
+                                                   head_offset=g)
+            assert torch.equal(sc[0, a:b], full[0][g, a:b])
+            assert torch.equal(po[0, a:b], full[1][g, a:b])
+            assert torch.equal(idx[0], full[2][g, a:b])
+            assert torch.equal(slots[:, 0], full[3][a:b, g])
+
+
+def test_streamed_shard_equals_full(dev):
+    """The streamed path on one rank's shard (host rows of one kv group, a token
+    window that does not start at a chunk edge) equals the same rows of the full path."""
+    from unum_ops_b200 import block_select, block_select_streamed
+
+    L = 16384
+    q, k, cu_q, cu_k, nk, table, tb, pos, sl = _c3_like(L, 12, dev)
+    full = block_select(q, k, cu_q, cu_k, nk, table, tb, pos, sl, max_context_len=L)
+    g, a, b = 1, 5184, 13760
+    q_host = q[a:b, 16 * g:16 * (g + 1)].contiguous().cpu().pin_memory()
+    res = torch.empty(1, b - a, 64, dtype=torch.int32).pin_memory()
+    sc, po, idx, slots = block_select_streamed(q_host, k[:, g:g + 1], cu_q, cu_k, nk, table, tb, pos, sl,
+                                               max_context_len=L, chunk_tokens=4096, result_host=res,
+                                               t_begin=a, head_offset=g)
+    torch.cuda.synchronize()
+    assert torch.equal(sc[0, a:b], full[0][g, a:b])
+    assert torch.equal(idx[0], full[2][g, a:b])
+    assert torch.equal(res[0], full[2][g, a:b].cpu())
+    assert torch.equal(slots[:, 0], full[3][a:b, g])
+
+
+def test_block_table_shard_into_full_output(dev, oracle_lib):
+    """get_block_table_shard writing one head's rows straight into the full
+    [T, Hk, K*64] output equals the unsharded call."""
+    from unum_ops_b200 import get_block_table_shard
+    from unum_ops_b200.sparse_kernel_extension import get_block_table_ref_torch
+
+    rng = np.random.default_rng(13)
+    T, K = 3000, 64
+    topk = rng.integers(-1, 40, size=(2, T, K)).astype(np.int32)
+    table = rng.permutation(1 << 16).astype(np.int32).reshape(16, 4096)
+    tb = rng.integers(0, 16, size=T).astype(np.int32)
+    pos = rng.integers(1, 4096, size=T).astype(np.int32)
+    sl = np.full(16, 4000, np.int32)
+    args = [_t(x, dev) for x in (table, tb, pos, sl)]
+    ref = get_block_table_ref_torch(_t(topk, dev), *args)
+    out = torch.zeros_like(ref)
+    for g in range(2):
+        get_block_table_shard(_t(topk[g:g + 1], dev), *args, head_offset=g, out=out[:, g:g + 1])
+    assert torch.equal(out, ref)

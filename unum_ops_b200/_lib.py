@@ -31,6 +31,8 @@ SIGNATURES = {
     "unum_abi_version": ([], _int),
     "unum_get_block_table": ([_p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _p,
                               _int, _p, _int, _i32, _p, _p], _int),
+    "unum_get_block_table_shard": ([_p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p,
+                                    _p, _int, _p, _int, _i32, _i64, _i64, _p, _p], _int),
     "unum_max_pooling_1d_varlen": ([_p, _int, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64,
                                     _i64, _i64, _i64, _p, _p], _int),
     "unum_topk_blocks": ([_p, _int, _i64, _i64, _i64, _i64, _p, _p], _int),

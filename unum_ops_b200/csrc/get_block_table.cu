@@ -28,7 +28,8 @@ get_block_table_kernel(const int32_t *__restrict__ topk, int64_t H, int64_t T, i
                        const int32_t *__restrict__ table, int64_t B, int64_t L, int64_t bt_stride,
                        const int32_t *__restrict__ token_to_bs, const int32_t *__restrict__ pos_in_bs,
                        int pos_scalar, const int32_t *__restrict__ seqlen, int seqlen_scalar,
-                       uint32_t head_group, bool vec_ok, int32_t *__restrict__ out) {
+                       uint32_t head_group, uint32_t h0, int64_t out_ts, bool vec_ok,
+                       int32_t *__restrict__ out) {
     const int lane = threadIdx.x & 31;
     const int64_t rows = T * H;
     const int32_t items = (int32_t)(K * (kBlock / 4));  // int4 items per row
@@ -37,15 +38,16 @@ get_block_table_kernel(const int32_t *__restrict__ topk, int64_t H, int64_t T, i
     for (int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); row < rows;
          row += (int64_t)gridDim.x * kWarps) {
         const int64_t t = row / H;
-        const uint32_t h = (uint32_t)(row - t * H);
+        const uint32_t hl = (uint32_t)(row - t * H);  // head within topk / out
+        const uint32_t h = hl + h0;                    // head index in the block-table values
         const int32_t bs = __ldg(token_to_bs + t);
         const bool bs_ok = bs >= 0 && bs < B;
         const int32_t lim_pos = pos_scalar ? __ldg(pos_in_bs) : __ldg(pos_in_bs + t);
         const int32_t sl = seqlen_scalar ? __ldg(seqlen) : (bs_ok ? __ldg(seqlen + bs) : 0);
         const int32_t lim = bs_ok ? min(lim_pos, sl) : INT32_MIN;  // valid iff 0 <= pos < lim
         const int32_t *trow = table + (bs_ok ? (int64_t)bs * bt_stride : 0);
-        const int32_t *tk = topk + (int64_t)h * ts_h + t * ts_t;
-        int4 *orow = reinterpret_cast<int4 *>(out) + row * items;
+        const int32_t *tk = topk + (int64_t)hl * ts_h + t * ts_t;
+        int4 *orow = reinterpret_cast<int4 *>(out + t * out_ts) + (int64_t)hl * items;
         for (int32_t e0 = 0; e0 < items; e0 += 32 * kUnroll) {
             int32_t p0[kUnroll];
 #pragma unroll
@@ -87,14 +89,12 @@ get_block_table_kernel(const int32_t *__restrict__ topk, int64_t H, int64_t T, i
 
 }  // namespace
 
-extern "C" int unum_get_block_table(const int32_t *topk_idx, int64_t H, int64_t T, int64_t K,
-                                    int64_t ts_h, int64_t ts_t, int64_t ts_k,
-                                    const int32_t *block_table, int64_t B, int64_t L,
-                                    int64_t bt_stride, const int32_t *token_to_bs,
-                                    const int32_t *token_pos_in_bs, int pos_is_scalar,
-                                    const int32_t *seqlen_q, int seqlen_is_scalar,
-                                    int32_t head_group, int32_t *out, void *stream) {
-    unum::clear_error();
+namespace {
+int launch_gbt(const int32_t *topk_idx, int64_t H, int64_t T, int64_t K, int64_t ts_h, int64_t ts_t,
+               int64_t ts_k, const int32_t *block_table, int64_t B, int64_t L, int64_t bt_stride,
+               const int32_t *token_to_bs, const int32_t *token_pos_in_bs, int pos_is_scalar,
+               const int32_t *seqlen_q, int seqlen_is_scalar, int32_t head_group, int64_t h0,
+               int64_t out_ts, int32_t *out, void *stream) {
     UNUM_CHECK_ARG(H >= 0 && T >= 0 && K >= 0 && B >= 0 && L >= 0, "negative size");
     if (H == 0 || T == 0 || K == 0) return UNUM_OK;
     UNUM_CHECK_ARG(topk_idx && token_to_bs && token_pos_in_bs && seqlen_q && out,
@@ -103,6 +103,9 @@ extern "C" int unum_get_block_table(const int32_t *topk_idx, int64_t H, int64_t 
     UNUM_CHECK_ARG(unum::aligned16(out), "out must be 16-byte aligned");
     UNUM_CHECK_ARG(K * kBlock <= (int64_t)INT32_MAX / 4, "K too large");
     UNUM_CHECK_ARG(L <= (int64_t)INT32_MAX, "block_table row too long");
+    UNUM_CHECK_ARG(h0 >= 0 && h0 <= (int64_t)INT32_MAX, "head offset out of range");
+    UNUM_CHECK_ARG(out_ts >= H * K * kBlock && out_ts % 4 == 0,
+                   "out token stride must cover H*K*64 ids and be a multiple of 4");
     const bool vec_ok = unum::aligned16(block_table) && (bt_stride % 4 == 0);
     const int64_t rows = T * H;
     const int64_t want = (rows + kWarps - 1) / kWarps;
@@ -110,7 +113,35 @@ extern "C" int unum_get_block_table(const int32_t *topk_idx, int64_t H, int64_t 
     const int grid = (int)(want < cap ? want : cap);
     get_block_table_kernel<<<grid, kWarps * 32, 0, (cudaStream_t)stream>>>(
         topk_idx, H, T, K, ts_h, ts_t, ts_k, block_table, B, L, bt_stride, token_to_bs,
-        token_pos_in_bs, pos_is_scalar, seqlen_q, seqlen_is_scalar, (uint32_t)head_group, vec_ok,
-        out);
+        token_pos_in_bs, pos_is_scalar, seqlen_q, seqlen_is_scalar, (uint32_t)head_group,
+        (uint32_t)h0, out_ts, vec_ok, out);
     return unum::check_launch("get_block_table_kernel");
+}
+}  // namespace
+
+extern "C" int unum_get_block_table(const int32_t *topk_idx, int64_t H, int64_t T, int64_t K,
+                                    int64_t ts_h, int64_t ts_t, int64_t ts_k,
+                                    const int32_t *block_table, int64_t B, int64_t L,
+                                    int64_t bt_stride, const int32_t *token_to_bs,
+                                    const int32_t *token_pos_in_bs, int pos_is_scalar,
+                                    const int32_t *seqlen_q, int seqlen_is_scalar,
+                                    int32_t head_group, int32_t *out, void *stream) {
+    unum::clear_error();
+    return launch_gbt(topk_idx, H, T, K, ts_h, ts_t, ts_k, block_table, B, L, bt_stride, token_to_bs,
+                      token_pos_in_bs, pos_is_scalar, seqlen_q, seqlen_is_scalar, head_group, 0,
+                      H * K * kBlock, out, stream);
+}
+
+extern "C" int unum_get_block_table_shard(const int32_t *topk_idx, int64_t H, int64_t T, int64_t K,
+                                          int64_t ts_h, int64_t ts_t, int64_t ts_k,
+                                          const int32_t *block_table, int64_t B, int64_t L,
+                                          int64_t bt_stride, const int32_t *token_to_bs,
+                                          const int32_t *token_pos_in_bs, int pos_is_scalar,
+                                          const int32_t *seqlen_q, int seqlen_is_scalar,
+                                          int32_t head_group, int64_t head_offset,
+                                          int64_t out_token_stride, int32_t *out, void *stream) {
+    unum::clear_error();
+    return launch_gbt(topk_idx, H, T, K, ts_h, ts_t, ts_k, block_table, B, L, bt_stride, token_to_bs,
+                      token_pos_in_bs, pos_is_scalar, seqlen_q, seqlen_is_scalar, head_group,
+                      head_offset, out_token_stride, out, stream);
 }

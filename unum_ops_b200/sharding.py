@@ -51,15 +51,17 @@ def plan_sequences(costs, n_ranks: int) -> list[list[int]]:
 
 
 def plan_query_ranges(q_len: int, k_len: int, n_parts: int, causal: bool = True,
-                      align: int = 64) -> list[tuple[int, int]]:
-    """Split [0, q_len) into n_parts contiguous ranges of near-equal stage-1 work.
+                      align: int = 64, token_cost: float = 1.0) -> list[tuple[int, int]]:
+    """Split [0, q_len) into n_parts contiguous ranges of near-equal work.
 
+    A query's work is its visible compressed keys (stage 1) plus ``token_cost``, the
+    per-token work of pooling, top-k and get_block_table in units of one visible key.
     Boundaries are multiples of ``align`` (a 64-token sparse block, so pooling's
     local-window rows never straddle shards) except the last.
     """
     if n_parts <= 0:
         raise ValueError("n_parts must be positive")
-    w = visible_counts(q_len, k_len, causal) + 1
+    w = visible_counts(q_len, k_len, causal) + float(token_cost)
     cum = np.concatenate([[0], np.cumsum(w)])
     total = cum[-1]
     bounds = [0]
