@@ -226,21 +226,13 @@ TOKEN_COST = 560.0
 
 
 def shard_of(world, rank, strong):
-    """(first kv head, kv heads, t_begin, t_end) this rank computes.
-
-    Strong scaling (config 3's sharding): with an even rank count each rank owns one
-    kv head and one of world/2 query ranges of equal work; otherwise both heads and
-    one of `world` ranges.  Weak scaling: the whole sequence (every rank its own)."""
-    from unum_ops_b200.sharding import plan_query_ranges
+    """(first kv head, kv heads, t_begin, t_end) this rank computes: config 3's kv head x
+    query range shard with strong scaling, the whole sequence with weak scaling."""
+    from unum_ops_b200.sharding import prefill_shard
 
     if world == 1 or not strong:
         return 0, HK, 0, L_SEQ
-    if world % HK == 0:
-        g, nh, n_r, r = rank % HK, 1, world // HK, rank // HK
-    else:
-        g, nh, n_r, r = 0, HK, world, rank
-    a, b = plan_query_ranges(L_SEQ, NKC, n_r, token_cost=TOKEN_COST)[r]
-    return g, nh, a, b
+    return prefill_shard(world, rank, L_SEQ, NKC, HK, token_cost=TOKEN_COST)
 
 
 def run_ours(args):

@@ -86,3 +86,19 @@ def test_two_rank_gloo_shard_and_gather(oracle_lib):
         p.join(timeout=120)
     assert all(p.exitcode == 0 for p in procs)
     assert ret.get(timeout=5) == 0.0
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_prefill_shards_cover_each_head_and_token_once(world):
+    from unum_ops_b200 import sharding
+
+    L = 131072
+    nk = (L - 32) // 16 + 1
+    cover = np.zeros((2, L), np.int32)
+    work = []
+    for r in range(world):
+        g, nh, a, b = sharding.prefill_shard(world, r, L, nk, 2, token_cost=560.0)
+        cover[g:g + nh, a:b] += 1
+        work.append((sharding.visible_counts(L, nk)[a:b] + 560.0).sum() * nh)
+    assert (cover == 1).all()
+    assert max(work) / min(work) < 1.05  # ranges of near-equal work

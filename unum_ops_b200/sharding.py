@@ -71,3 +71,20 @@ def plan_query_ranges(q_len: int, k_len: int, n_parts: int, causal: bool = True,
         bounds.append(min(max(t, bounds[-1]), q_len))
     bounds.append(q_len)
     return [(bounds[i], bounds[i + 1]) for i in range(n_parts)]
+
+
+def prefill_shard(world: int, rank: int, q_len: int, k_len: int, n_kv_heads: int = 2,
+                  causal: bool = True, token_cost: float = 1.0) -> tuple[int, int, int, int]:
+    """The (first kv head, kv heads, t_begin, t_end) shard of one long sequence that
+    rank ``rank`` of ``world`` computes: with a rank count divisible by the kv heads,
+    each rank owns one kv head and one of world / n_kv_heads query ranges of equal work
+    (``plan_query_ranges``); otherwise every kv head and one of ``world`` ranges.  The
+    shards of all ranks cover every (kv head, query) exactly once."""
+    if not 0 <= rank < world:
+        raise ValueError("rank outside [0, world)")
+    if world % n_kv_heads == 0:
+        g, nh, n_r, r = rank % n_kv_heads, 1, world // n_kv_heads, rank // n_kv_heads
+    else:
+        g, nh, n_r, r = 0, n_kv_heads, world, rank
+    a, b = plan_query_ranges(q_len, k_len, n_r, causal, token_cost=token_cost)[r]
+    return g, nh, a, b
