@@ -461,3 +461,47 @@ def test_block_table_shard_into_full_output(dev, oracle_lib):
     for g in range(2):
         get_block_table_shard(_t(topk[g:g + 1], dev), *args, head_offset=g, out=out[:, g:g + 1])
     assert torch.equal(out, ref)
+
+
+# ---------------------------------------------------------------- stage 1, decode kernel
+@pytest.mark.parametrize("c", [c for c in cases.stage1_cases() if c["q"].shape[1] // c["k"].shape[1] >= 16],
+                         ids=lambda c: c["name"])
+def test_stage1_decode_kernel_matches_reference(c, dev, oracle_lib, monkeypatch):
+    """The per-(token, kv head) decode kernel, forced on every fixture it can run (it is
+    chosen by default for one or a few queries per sequence), against the reference's
+    outputs and the oracle."""
+    monkeypatch.setenv("UNUM_STAGE1_PATH", "decode")
+    out = _stage1(c, dev).float().cpu().numpy()
+    ref = _bf16_to_f32(_npz("stage1.npz")[c["name"] + "/out_bf16"])
+    orc = oracle_lib.stage1(c["q"], c["k"], c["cu_q"], c["cu_k"], c["causal"])
+    np.testing.assert_allclose(out, orc, atol=ATOL, rtol=RTOL)
+    np.testing.assert_allclose(out, ref, atol=2 * ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("hq", [32, 64])
+@pytest.mark.parametrize("causal", [True, False])
+def test_stage1_decode_kernel_varlen(hq, causal, dev, oracle_lib):
+    """Decode-shaped batches through the default dispatch: empty sequences, one to a
+    few query tokens, contexts from one key to the most a row holds (G=32: 2048,
+    G=16: 4096), and a token window."""
+    from unum_ops_b200.infllm_v2 import infllmv2_attn_stage1, stage1_status
+
+    rng = np.random.default_rng(21 + hq)
+    B = 40
+    q_lens = rng.integers(0, 3, size=B)
+    q_lens[:4] = [1, 0, 2, 1]
+    max_k = 4096 if hq == 32 else 2048
+    k_lens = rng.integers(1, max_k + 1, size=B)
+    k_lens[:4] = [1, 7, max_k, 128]
+    T, Tk = int(q_lens.sum()), int(k_lens.sum())
+    q = rng.standard_normal((T, hq, 128), dtype=np.float32)
+    k = rng.standard_normal((Tk, 2, 128), dtype=np.float32)
+    qb, kb = _t(q, dev, torch.bfloat16), _t(k, dev, torch.bfloat16)
+    cu_q, cu_k = cases.cu(q_lens), cases.cu(k_lens)
+    out = infllmv2_attn_stage1(qb, kb, None, _t(cu_q, dev), _t(cu_k, dev), max_seqlen_k=max_k,
+                               causal=causal)
+    torch.cuda.synchronize()
+    assert stage1_status(dev) == 0
+    orc = oracle_lib.stage1(qb.float().cpu().numpy(), kb.float().cpu().numpy(), cu_q, cu_k, causal,
+                            out_stride=out.shape[-1])
+    np.testing.assert_allclose(out.float().cpu().numpy(), orc, atol=ATOL, rtol=RTOL)

@@ -37,6 +37,9 @@
 // issuing TMA/UMMA work, runs its remaining loops without waiting, frees TMEM
 // and returns, so the context stays usable and the host sees the status.
 #include <cuda.h>
+#include <cstdlib>
+#include <cstring>
+
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 
@@ -83,7 +86,8 @@ constexpr uint32_t kIdescP2 = idesc_bf16_f32(128, 256);
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint64_t kWaitNs = 1000000000ull;  // bounded wait: 1 s
 
-// workspace layout (int32 words): [0] status, [1..3] reserved, [4..4+n_seq] tile prefix
+// workspace layout (int32 words): [0] status, [1] decode work counter, [2..3] reserved,
+// [4..4+n_seq] tile prefix
 constexpr int kWsTiles = 4;
 
 struct Params {
@@ -738,6 +742,7 @@ stage1_prologue(const int32_t *__restrict__ cu_q, int32_t n_seq, int32_t QT, int
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) {
         ws[0] = 0;
+        ws[1] = 0;  // work counter of the decode kernel
         carry_s = 0;
     }
     __syncthreads();
@@ -846,6 +851,360 @@ int launch_main(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap 
     return unum::check_launch("stage1_kernel");
 }
 
+// ------------------------------------------------------------------ decode kernel
+// Stage 1 with one work item per (query token, kv head): the path for decode
+// batches (one or a few query tokens per sequence), where the tile kernel above
+// would fill 1 of 256/G rows of each tile and re-read every key tile in its
+// second pass.  Here each 128-key tile of the token's visible keys is one MMA
+// M=128 (keys) x N=G (the token's query heads) x K=128, and all the item's tiles
+// stay in TMEM side by side (G columns each, up to 512/G tiles), so the keys are
+// read from HBM once and the softmax needs no second MMA pass: the epilogue reads
+// the scores from TMEM three times (max, sum, output).  The path is HBM-bound on
+// the compressed keys.  Items are taken from a work counter (workspace word 1,
+// zeroed by the prologue), so CTAs stay balanced although items differ in size.
+constexpr int kDecStages = 4;        // K ring depth
+constexpr int kDecSlots = 4;         // item queue depth (an item = its id + its q tile)
+constexpr int kDecEpiWarps = 4;      // 128 epilogue threads = TMEM lanes = keys of a tile
+constexpr int kDecProducerWarp = 4;
+constexpr int kDecMmaWarp = 5;
+constexpr int kDecThreads = 6 * 32;
+constexpr int kDecEpiBarrier = 1;
+constexpr uint32_t kDecQSlot = 2 * 32 * 128;                 // two 64-column panels of up to 32 heads
+constexpr uint32_t kDecOffK = kDecSlots * kDecQSlot;          // 32 KB
+constexpr uint32_t kDecOffRed = kDecOffK + kDecStages * kKStage;
+constexpr uint32_t kDecOffBar = kDecOffRed + 2 * kDecEpiWarps * 32 * 4;
+// barriers: item_full, item_empty, q_full (per slot), k_full, k_empty (per stage), tmem_full, tmem_empty
+constexpr uint32_t kDecNumBars = 3 * kDecSlots + 2 * kDecStages + 2;
+constexpr uint32_t kDecOffMisc = kDecOffBar + kDecNumBars * 8;  // item ids, abort flag, TMEM address
+constexpr uint32_t kDecSmemBytes = kDecOffMisc + 64 + 1024;
+static_assert(kDecOffK % 1024 == 0 && kDecQSlot % 1024 == 0, "SW128 operand tiles need 1024-byte alignment");
+static_assert(kDecSmemBytes <= 232448, "exceeds the 227 KB of shared memory a CTA may use");
+
+// N = 16 or 32 consecutive f32 columns of this thread's TMEM lane.
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[N]);
+template <>
+__device__ __forceinline__ void tmem_ld_cols<16>(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+template <>
+__device__ __forceinline__ void tmem_ld_cols<32>(uint32_t taddr, float (&v)[32]) {
+    tmem_ld32(taddr, v);
+}
+
+// What one decode item covers.
+struct DecItem {
+    int32_t g;        // kv head
+    int64_t t;        // query token
+    int32_t vis;      // visible compressed keys
+    int32_t nkt;      // key tiles
+    int64_t k_start;  // first compressed key of the token's sequence
+    bool active;      // false: token outside every sequence or outside the token window
+};
+
+// An item needing more than max_tiles key tiles (more visible keys than the
+// out_stride the caller sized the output for allows) gets nkt = 0, vis = -1:
+// nothing is computed and the epilogue reports it in the status word.
+__device__ __forceinline__ DecItem dec_decode(int64_t w, const Params &p, int32_t max_tiles) {
+    DecItem it;
+    it.g = (int32_t)(w % p.Hk);
+    it.t = w / p.Hk;
+    it.active = false;
+    it.vis = 0;
+    it.nkt = 0;
+    it.k_start = 0;
+    if (p.n_seq <= 0 || it.t < p.t_begin || it.t >= p.t_end) return it;
+    const int32_t t = (int32_t)it.t;
+    if (t < __ldg(p.cu_q) || t >= __ldg(p.cu_q + p.n_seq)) return it;
+    int32_t lo = 0, hi = p.n_seq;  // largest b with cu_q[b] <= t
+    while (hi - lo > 1) {
+        const int32_t mid = (lo + hi) >> 1;
+        if (__ldg(p.cu_q + mid) <= t) lo = mid; else hi = mid;
+    }
+    const int32_t qs = __ldg(p.cu_q + lo);
+    const int32_t q_len = __ldg(p.cu_q + lo + 1) - qs;
+    it.k_start = __ldg(p.cu_k + lo);
+    const int32_t k_len = __ldg(p.cu_k + lo + 1) - (int32_t)it.k_start;
+    it.vis = visible(t - qs, q_len, k_len, p.causal);
+    it.nkt = (it.vis + kBN - 1) / kBN;
+    if (it.nkt > max_tiles) {
+        it.nkt = 0;
+        it.vis = -1;
+    }
+    it.active = true;
+    return it;
+}
+
+// Warp-wide max (or sum) of each of N per-thread values, then across the 4
+// epilogue warps through shared memory; every epilogue thread gets the results.
+template <int N, bool kMax>
+__device__ __forceinline__ void dec_reduce(float (&v)[N], float *red, int warp, int lane) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float y = __shfl_xor_sync(0xffffffffu, v[i], o);
+            v[i] = kMax ? fmaxf(v[i], y) : v[i] + y;
+        }
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) red[warp * 32 + i] = v[i];
+    }
+    named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        float a = red[i];
+#pragma unroll
+        for (int w2 = 1; w2 < kDecEpiWarps; ++w2) a = kMax ? fmaxf(a, red[w2 * 32 + i]) : a + red[w2 * 32 + i];
+        v[i] = a;
+    }
+}
+
+// Named barrier over n threads that also ORs a predicate across them, so a
+// decision taken after it (leave the loop) is the same in every thread.
+__device__ __forceinline__ bool named_bar_or(int id, int n, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.or.pred p, %2, %3, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r) : "r"((uint32_t)pred), "r"(id), "r"(n) : "memory");
+    return r != 0;
+}
+
+template <int G>
+__global__ void __launch_bounds__(kDecThreads, 1)
+stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ Params p) {
+    constexpr uint32_t kQPanelD = G * 128;        // one 64-column panel of the token's G heads
+    constexpr uint32_t kQBytesD = 2 * kQPanelD;
+    constexpr uint32_t kIdesc = idesc_bf16_f32(128, G);
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t sbase = (raw + 1023u) & ~1023u;
+    uint8_t *sgen = smem_raw + (sbase - raw);
+    float *red = reinterpret_cast<float *>(sgen + kDecOffRed);  // [2][4 warps][32]
+    const uint32_t bar0 = sbase + kDecOffBar;
+    const uint32_t item_full = bar0, item_empty = bar0 + 8 * kDecSlots, q_full = bar0 + 16 * kDecSlots;
+    const uint32_t k_full = bar0 + 24 * kDecSlots, k_empty = k_full + 8 * kDecStages;
+    const uint32_t tmem_full = k_empty + 8 * kDecStages, tmem_empty = tmem_full + 8;
+    volatile int64_t *item_id = reinterpret_cast<volatile int64_t *>(sgen + kDecOffMisc);  // [kDecSlots]
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(sgen + kDecOffMisc + 8 * kDecSlots);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sgen + kDecOffMisc + 8 * kDecSlots + 16);
+    Sync sy;
+    sy.abort = abort_flag;
+    sy.status = p.ws;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kDecSlots; ++i) {
+            mbar_init(item_full + 8 * i, 1);
+            mbar_init(item_empty + 8 * i, 2);  // the MMA warp's commit + the epilogue
+            mbar_init(q_full + 8 * i, 1);
+        }
+        for (int i = 0; i < kDecStages; ++i) {
+            mbar_init(k_full + 8 * i, 1);
+            mbar_init(k_empty + 8 * i, 1);
+        }
+        mbar_init(tmem_full, 1);
+        mbar_init(tmem_empty, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == kDecProducerWarp && lane == 0) {
+        prefetch_tmap(&tmQ);
+        prefetch_tmap(&tmK);
+    }
+    if (warp == kDecMmaWarp) {
+        tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int64_t n_items = p.T * p.Hk;
+    int32_t *counter = p.ws + 1;
+
+    if (warp == kDecProducerWarp) {
+        if (lane == 0) {
+            uint32_t kc = 0;
+            for (uint32_t n = 0;; ++n) {
+                const uint32_t s = n % kDecSlots;
+                if (!wait_bar(sy, item_empty + 8 * s, ((n / kDecSlots) & 1) ^ 1, 11)) break;
+                int64_t w = atomicAdd(counter, 1);
+                if (w >= n_items) w = -1;
+                const DecItem it = w >= 0 ? dec_decode(w, p, (int32_t)kTmemCols / G) : DecItem{};
+                item_id[s] = w;
+                if (w >= 0 && it.nkt > 0) {
+                    mbar_arrive_expect_tx(q_full + 8 * s, kQBytesD);
+                    const uint32_t qd = sbase + s * kDecQSlot;
+                    tma_load_3d(qd, &tmQ, 0, it.g * G, (int32_t)it.t, q_full + 8 * s);
+                    tma_load_3d(qd + kQPanelD, &tmQ, 64, it.g * G, (int32_t)it.t, q_full + 8 * s);
+                } else if (w >= 0) {
+                    mbar_arrive(q_full + 8 * s);  // no keys: still one phase per use of the slot
+                }
+                mbar_arrive(item_full + 8 * s);
+                if (w < 0) break;
+                for (int32_t kt = 0; kt < it.nkt; ++kt, ++kc) {
+                    const uint32_t st = kc % kDecStages, ph = (kc / kDecStages) & 1;
+                    if (!wait_bar(sy, k_empty + 8 * st, ph ^ 1, 12)) break;
+                    const uint32_t dst = sbase + kDecOffK + st * kKStage;
+                    const int32_t krow = (int32_t)(it.k_start + (int64_t)kt * kBN);
+                    mbar_arrive_expect_tx(k_full + 8 * st, kKStage);
+                    tma_load_3d(dst, &tmK, 0, it.g, krow, k_full + 8 * st);
+                    tma_load_3d(dst + kKPanel, &tmK, 64, it.g, krow, k_full + 8 * st);
+                }
+                if (*abort_flag) break;
+            }
+        }
+    } else if (warp == kDecMmaWarp) {
+        if (lane == 0) {
+            uint32_t kc = 0, tn = 0;
+            for (uint32_t n = 0;; ++n) {
+                const uint32_t s = n % kDecSlots, sph = (n / kDecSlots) & 1;
+                if (!wait_bar(sy, item_full + 8 * s, sph, 13)) break;
+                const int64_t w = item_id[s];
+                if (w < 0) break;
+                const DecItem it = dec_decode(w, p, (int32_t)kTmemCols / G);
+                if (it.nkt == 0) {
+                    mbar_arrive(item_empty + 8 * s);
+                    continue;
+                }
+                bool ok = wait_bar(sy, tmem_empty, (tn & 1) ^ 1, 14);
+                ok = ok && wait_bar(sy, q_full + 8 * s, sph, 15);
+                tc_fence_after();
+                const uint32_t qb = sbase + s * kDecQSlot;
+                for (int32_t kt = 0; ok && kt < it.nkt; ++kt, ++kc) {
+                    const uint32_t st = kc % kDecStages;
+                    ok = wait_bar(sy, k_full + 8 * st, (kc / kDecStages) & 1, 16);
+                    tc_fence_after();
+                    if (!ok) break;
+                    const uint32_t kb = sbase + kDecOffK + st * kKStage;
+#pragma unroll
+                    for (int kk = 0; kk < kD / 16; ++kk) {
+                        const uint32_t koff = (kk >> 2) * kKPanel + (kk & 3) * 32;
+                        const uint32_t qoff = (kk >> 2) * kQPanelD + (kk & 3) * 32;
+                        umma_bf16(tmem + kt * G, desc_kmajor_sw128(kb + koff), desc_kmajor_sw128(qb + qoff),
+                                  kIdesc, kk > 0);
+                    }
+                    umma_commit(k_empty + 8 * st);
+                }
+                if (!ok) break;
+                umma_commit(tmem_full);
+                umma_commit(item_empty + 8 * s);  // the q tile is free once the MMAs are done
+                ++tn;
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        // thread tid = TMEM lane = key tid of every tile; tile kt sits in columns kt*G..
+        const int tid = threadIdx.x;  // 0..127
+        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        const float c = p.c;
+        uint32_t tn = 0;
+        for (uint32_t n = 0;; ++n) {
+            const uint32_t s = n % kDecSlots;
+            const bool bad = !wait_bar(sy, item_full + 8 * s, (n / kDecSlots) & 1, 17);
+            if (named_bar_or(kDecEpiBarrier, kDecEpiWarps * 32, bad)) break;  // gave up: all leave
+            const int64_t w = item_id[s];
+            if (w < 0) break;
+            const DecItem it = dec_decode(w, p, (int32_t)kTmemCols / G);
+            if (it.vis < 0 && tid == 0) atomicCAS(p.ws, 0, 20);  // more keys than out_stride holds
+            __nv_bfloat16 *orow = p.out + ((int64_t)it.g * p.T + it.t) * p.out_stride;
+            int32_t zero_from = 0;  // first column of the row to zero-fill
+            if (it.active && it.nkt > 0) {
+                const bool bad2 = !wait_bar(sy, tmem_full, tn & 1, 18);
+                if (named_bar_or(kDecEpiBarrier, kDecEpiWarps * 32, bad2)) break;
+                tc_fence_after();
+                float v[G], m[G], l[G];
+#pragma unroll
+                for (int i = 0; i < G; ++i) m[i] = -INFINITY;
+                for (int32_t kt = 0; kt < it.nkt; ++kt) {
+                    tmem_ld_cols<G>(tmem + lane_base + kt * G, v);
+                    tmem_wait_ld();
+                    if (kt * kBN + tid < it.vis) {
+#pragma unroll
+                        for (int i = 0; i < G; ++i) m[i] = fmaxf(m[i], v[i]);
+                    }
+                }
+                dec_reduce<G, true>(m, red, warp, lane);
+#pragma unroll
+                for (int i = 0; i < G; ++i) l[i] = 0.f;
+                for (int32_t kt = 0; kt < it.nkt; ++kt) {
+                    tmem_ld_cols<G>(tmem + lane_base + kt * G, v);
+                    tmem_wait_ld();
+                    if (kt * kBN + tid < it.vis) {
+#pragma unroll
+                        for (int i = 0; i < G; ++i) l[i] += ex2((v[i] - m[i]) * c);
+                    }
+                }
+                dec_reduce<G, false>(l, red + kDecEpiWarps * 32, warp, lane);
+#pragma unroll
+                for (int i = 0; i < G; ++i) m[i] = fmaf(m[i], c, log2f(l[i]));  // b = m*c + log2(l)
+                for (int32_t kt = 0; kt < it.nkt; ++kt) {
+                    tmem_ld_cols<G>(tmem + lane_base + kt * G, v);
+                    tmem_wait_ld();
+                    const int32_t j = kt * kBN + tid;
+                    float o = 0.f;
+                    if (j < it.vis) {
+#pragma unroll
+                        for (int i = 0; i < G; ++i) o += ex2(fmaf(v[i], c, -m[i]));
+                        o = fmaxf(o, 0.f);  // NaN scores give 0, as in the tile kernel
+                    }
+                    if (j < p.out_stride) orow[j] = __float2bfloat16_rn(o);
+                }
+                tc_fence_before();
+                named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);  // every TMEM read of the item done
+                if (tid == 0) mbar_arrive(tmem_empty);
+                ++tn;
+                zero_from = it.nkt * kBN;
+            } else {
+                named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);  // every thread has read item_id[s]
+            }
+            if (tid == 0) mbar_arrive(item_empty + 8 * s);
+            if (it.active && it.vis >= 0 && zero_from < p.out_stride) {
+                const int32_t n16 = (int32_t)((p.out_stride - zero_from) >> 3);
+                uint4 *dst = reinterpret_cast<uint4 *>(orow + zero_from);
+                for (int32_t e = tid; e < n16; e += kDecEpiWarps * 32) dst[e] = make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kDecMmaWarp) {
+        if (*abort_flag) {
+            // give TMA/UMMA work already in flight time to land before TMEM is released
+            const uint64_t t0 = globaltimer_ns();
+            while (globaltimer_ns() - t0 < 2000000ull) {
+            }
+        }
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+template <int G>
+int launch_decode(const CUtensorMap &mq, const CUtensorMap &mk, const Params &p, cudaStream_t s) {
+    auto kern = stage1_decode_kernel<G>;
+    UNUM_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecSmemBytes));
+    const int64_t items = p.T * p.Hk;
+    const int64_t sms = unum::sm_count();
+    const int grid = (int)(items < sms ? items : sms);
+    kern<<<grid, kDecThreads, kDecSmemBytes, s>>>(mq, mk, p);
+    return unum::check_launch("stage1_decode_kernel");
+}
+
 }  // namespace
 
 extern "C" size_t unum_stage1_workspace_size(int64_t n_seq) {
@@ -854,6 +1213,20 @@ extern "C" size_t unum_stage1_workspace_size(int64_t n_seq) {
 }
 
 namespace {
+
+// Which kernel computes stage 1: the decode kernel for batches of (nearly) one
+// query token per sequence when its shape fits (no fused pooling, G of 16 or 32, a
+// row's key tiles fit TMEM); otherwise the tile kernel.  UNUM_STAGE1_PATH=tile or
+// =decode forces one (where the decode kernel can run), for testing.
+bool use_decode_kernel(int64_t G, int64_t T, int64_t n_seq, int64_t out_stride, const void *pooled) {
+    const bool fits = pooled == nullptr && (G == 16 || G == 32) &&
+                      out_stride <= (int64_t)kBN * ((int64_t)kTmemCols / G);
+    if (!fits) return false;
+    const char *env = getenv("UNUM_STAGE1_PATH");
+    if (env && strcmp(env, "tile") == 0) return false;
+    if (env && strcmp(env, "decode") == 0) return true;
+    return T <= 4 * n_seq;
+}
 
 int stage1_run(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, int64_t q_sh,
                const void *k, int64_t Tk, int64_t Hk, int64_t k_st, int64_t k_sh,
@@ -911,6 +1284,30 @@ int stage1_run(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, in
     if (int rc = make_map(&mk, k, (uint64_t)D, (uint64_t)Hk, (uint64_t)Tk, (uint64_t)k_sh * 2,
                           (uint64_t)k_st * 2, 1, kBN))
         return rc;
+    if (use_decode_kernel(G, T, n_seq, out_stride, pooled)) {
+        CUtensorMap mqd;  // q with one token's G heads per box
+        if (int rc = make_map(&mqd, q, (uint64_t)D, (uint64_t)Hq, (uint64_t)T, (uint64_t)q_sh * 2,
+                              (uint64_t)q_st * 2, (uint32_t)G, 1))
+            return rc;
+        Params p;
+        p.cu_q = cu_seqlens_q;
+        p.cu_k = cu_seqlens_k;
+        p.ws = ws;
+        p.out = (__nv_bfloat16 *)out;
+        p.T = T;
+        p.out_stride = out_stride;
+        p.n_seq = (int32_t)n_seq;
+        p.Hk = (int32_t)Hk;
+        p.causal = causal ? 1 : 0;
+        p.c = softmax_scale * kLog2e;
+        p.pooled = nullptr;
+        p.NB = 0;
+        p.init_blocks = 0;
+        p.local_blocks = 0;
+        p.t_begin = t_begin;
+        p.t_end = t_end;
+        return G == 16 ? launch_decode<16>(mqd, mk, p, s) : launch_decode<32>(mqd, mk, p, s);
+    }
     CUtensorMap mo;  // out as a 2-D [Hk*T, out_stride] bf16 tensor, [64/G x 128] store boxes
     {
         auto enc = get_encode_fn();
