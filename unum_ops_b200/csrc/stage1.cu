@@ -860,7 +860,8 @@ int launch_main(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap 
 // stay in TMEM side by side (G columns each, up to 512/G tiles), so the keys are
 // read from HBM once and the softmax needs no second MMA pass: the epilogue reads
 // the scores from TMEM three times (max, sum, output).  The path is HBM-bound on
-// the compressed keys.  Items are taken from a work counter (workspace word 1,
+// the compressed keys.  TMEM is a ring of 512/G tile slots released tile by
+// tile, so consecutive items overlap.  Items are taken from a work counter (workspace word 1,
 // zeroed by the prologue), so CTAs stay balanced although items differ in size.
 constexpr int kDecStages = 4;        // K ring depth
 constexpr int kDecSlots = 4;         // item queue depth (an item = its id + its q tile)
@@ -873,8 +874,10 @@ constexpr uint32_t kDecQSlot = 2 * 32 * 128;                 // two 64-column pa
 constexpr uint32_t kDecOffK = kDecSlots * kDecQSlot;          // 32 KB
 constexpr uint32_t kDecOffRed = kDecOffK + kDecStages * kKStage;
 constexpr uint32_t kDecOffBar = kDecOffRed + 2 * kDecEpiWarps * 32 * 4;
-// barriers: item_full, item_empty, q_full (per slot), k_full, k_empty (per stage), tmem_full, tmem_empty
-constexpr uint32_t kDecNumBars = 3 * kDecSlots + 2 * kDecStages + 2;
+// barriers: item_full, item_empty, q_full, tmem_full (per item slot), k_full, k_empty (per
+// stage), and one per TMEM tile slot (free again)
+constexpr int kDecTmemSlotsMax = 32;  // 512 columns / 16 heads
+constexpr uint32_t kDecNumBars = 4 * kDecSlots + 2 * kDecStages + kDecTmemSlotsMax;
 constexpr uint32_t kDecOffMisc = kDecOffBar + kDecNumBars * 8;  // item ids, abort flag, TMEM address
 constexpr uint32_t kDecSmemBytes = kDecOffMisc + 64 + 1024;
 static_assert(kDecOffK % 1024 == 0 && kDecQSlot % 1024 == 0, "SW128 operand tiles need 1024-byte alignment");
@@ -997,7 +1000,11 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
     const uint32_t bar0 = sbase + kDecOffBar;
     const uint32_t item_full = bar0, item_empty = bar0 + 8 * kDecSlots, q_full = bar0 + 16 * kDecSlots;
     const uint32_t k_full = bar0 + 24 * kDecSlots, k_empty = k_full + 8 * kDecStages;
-    const uint32_t tmem_full = k_empty + 8 * kDecStages, tmem_empty = tmem_full + 8;
+    // TMEM is a ring of kTs tile slots of G columns; tile i of this CTA's stream uses slot
+    // i % kTs, so the next item's MMAs can start while the epilogue still reads this one
+    constexpr uint32_t kTs = kTmemCols / G;
+    // tmem_full per item slot: reusing a slot waits for item_empty, so no phase is overrun
+    const uint32_t tmem_full = k_empty + 8 * kDecStages, slot_empty = tmem_full + 8 * kDecSlots;
     volatile int64_t *item_id = reinterpret_cast<volatile int64_t *>(sgen + kDecOffMisc);  // [kDecSlots]
     volatile int *abort_flag = reinterpret_cast<volatile int *>(sgen + kDecOffMisc + 8 * kDecSlots);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sgen + kDecOffMisc + 8 * kDecSlots + 16);
@@ -1015,8 +1022,8 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
             mbar_init(k_full + 8 * i, 1);
             mbar_init(k_empty + 8 * i, 1);
         }
-        mbar_init(tmem_full, 1);
-        mbar_init(tmem_empty, 1);
+        for (int i = 0; i < kDecSlots; ++i) mbar_init(tmem_full + 8 * i, 1);
+        for (uint32_t i = 0; i < kTs; ++i) mbar_init(slot_empty + 8 * i, kDecEpiWarps);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -1069,7 +1076,7 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
         }
     } else if (warp == kDecMmaWarp) {
         if (lane == 0) {
-            uint32_t kc = 0, tn = 0;
+            uint32_t kc = 0, tc = 0;  // K stages used, TMEM tiles used
             for (uint32_t n = 0;; ++n) {
                 const uint32_t s = n % kDecSlots, sph = (n / kDecSlots) & 1;
                 if (!wait_bar(sy, item_full + 8 * s, sph, 13)) break;
@@ -1077,16 +1084,17 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                 if (w < 0) break;
                 const DecItem it = dec_decode(w, p, (int32_t)kTmemCols / G);
                 if (it.nkt == 0) {
+                    mbar_arrive(tmem_full + 8 * s);  // one phase per use of the slot
                     mbar_arrive(item_empty + 8 * s);
                     continue;
                 }
-                bool ok = wait_bar(sy, tmem_empty, (tn & 1) ^ 1, 14);
-                ok = ok && wait_bar(sy, q_full + 8 * s, sph, 15);
+                bool ok = wait_bar(sy, q_full + 8 * s, sph, 15);
                 tc_fence_after();
                 const uint32_t qb = sbase + s * kDecQSlot;
-                for (int32_t kt = 0; ok && kt < it.nkt; ++kt, ++kc) {
-                    const uint32_t st = kc % kDecStages;
-                    ok = wait_bar(sy, k_full + 8 * st, (kc / kDecStages) & 1, 16);
+                for (int32_t kt = 0; ok && kt < it.nkt; ++kt, ++kc, ++tc) {
+                    const uint32_t st = kc % kDecStages, slot = tc % kTs;
+                    ok = wait_bar(sy, slot_empty + 8 * slot, ((tc / kTs) & 1) ^ 1, 14);
+                    ok = ok && wait_bar(sy, k_full + 8 * st, (kc / kDecStages) & 1, 16);
                     tc_fence_after();
                     if (!ok) break;
                     const uint32_t kb = sbase + kDecOffK + st * kKStage;
@@ -1094,24 +1102,24 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                     for (int kk = 0; kk < kD / 16; ++kk) {
                         const uint32_t koff = (kk >> 2) * kKPanel + (kk & 3) * 32;
                         const uint32_t qoff = (kk >> 2) * kQPanelD + (kk & 3) * 32;
-                        umma_bf16(tmem + kt * G, desc_kmajor_sw128(kb + koff), desc_kmajor_sw128(qb + qoff),
+                        umma_bf16(tmem + slot * G, desc_kmajor_sw128(kb + koff), desc_kmajor_sw128(qb + qoff),
                                   kIdesc, kk > 0);
                     }
                     umma_commit(k_empty + 8 * st);
                 }
                 if (!ok) break;
-                umma_commit(tmem_full);
+                umma_commit(tmem_full + 8 * s);
                 umma_commit(item_empty + 8 * s);  // the q tile is free once the MMAs are done
-                ++tn;
             }
         }
     } else {
         // ------------------------------------------------------------ epilogue
-        // thread tid = TMEM lane = key tid of every tile; tile kt sits in columns kt*G..
+        // thread tid = TMEM lane = key tid of every tile; tile kt of an item sits in ring slot
+        // (tbase + kt) % kTs, columns slot*G..
         const int tid = threadIdx.x;  // 0..127
         const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
         const float c = p.c;
-        uint32_t tn = 0;
+        uint32_t tbase = 0;  // TMEM tiles consumed
         for (uint32_t n = 0;; ++n) {
             const uint32_t s = n % kDecSlots;
             const bool bad = !wait_bar(sy, item_full + 8 * s, (n / kDecSlots) & 1, 17);
@@ -1123,14 +1131,14 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
             __nv_bfloat16 *orow = p.out + ((int64_t)it.g * p.T + it.t) * p.out_stride;
             int32_t zero_from = 0;  // first column of the row to zero-fill
             if (it.active && it.nkt > 0) {
-                const bool bad2 = !wait_bar(sy, tmem_full, tn & 1, 18);
+                const bool bad2 = !wait_bar(sy, tmem_full + 8 * s, (n / kDecSlots) & 1, 18);
                 if (named_bar_or(kDecEpiBarrier, kDecEpiWarps * 32, bad2)) break;
                 tc_fence_after();
                 float v[G], m[G], l[G];
 #pragma unroll
                 for (int i = 0; i < G; ++i) m[i] = -INFINITY;
                 for (int32_t kt = 0; kt < it.nkt; ++kt) {
-                    tmem_ld_cols<G>(tmem + lane_base + kt * G, v);
+                    tmem_ld_cols<G>(tmem + lane_base + ((tbase + kt) % kTs) * G, v);
                     tmem_wait_ld();
                     if (kt * kBN + tid < it.vis) {
 #pragma unroll
@@ -1141,7 +1149,7 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
 #pragma unroll
                 for (int i = 0; i < G; ++i) l[i] = 0.f;
                 for (int32_t kt = 0; kt < it.nkt; ++kt) {
-                    tmem_ld_cols<G>(tmem + lane_base + kt * G, v);
+                    tmem_ld_cols<G>(tmem + lane_base + ((tbase + kt) % kTs) * G, v);
                     tmem_wait_ld();
                     if (kt * kBN + tid < it.vis) {
 #pragma unroll
@@ -1152,8 +1160,12 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
 #pragma unroll
                 for (int i = 0; i < G; ++i) m[i] = fmaf(m[i], c, log2f(l[i]));  // b = m*c + log2(l)
                 for (int32_t kt = 0; kt < it.nkt; ++kt) {
-                    tmem_ld_cols<G>(tmem + lane_base + kt * G, v);
+                    tmem_ld_cols<G>(tmem + lane_base + ((tbase + kt) % kTs) * G, v);
                     tmem_wait_ld();
+                    // this warp's last read of the tile: its slot may take a new tile
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(slot_empty + 8 * ((tbase + kt) % kTs));
                     const int32_t j = kt * kBN + tid;
                     float o = 0.f;
                     if (j < it.vis) {
@@ -1163,10 +1175,8 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                     }
                     if (j < p.out_stride) orow[j] = __float2bfloat16_rn(o);
                 }
-                tc_fence_before();
-                named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);  // every TMEM read of the item done
-                if (tid == 0) mbar_arrive(tmem_empty);
-                ++tn;
+                named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);  // every thread has read item_id[s]
+                tbase += (uint32_t)it.nkt;
                 zero_from = it.nkt * kBN;
             } else {
                 named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);  // every thread has read item_id[s]
