@@ -505,3 +505,32 @@ def test_stage1_decode_kernel_varlen(hq, causal, dev, oracle_lib):
     orc = oracle_lib.stage1(qb.float().cpu().numpy(), kb.float().cpu().numpy(), cu_q, cu_k, causal,
                             out_stride=out.shape[-1])
     np.testing.assert_allclose(out.float().cpu().numpy(), orc, atol=ATOL, rtol=RTOL)
+
+
+def test_block_select_graph_replays_new_inputs(dev):
+    """BlockSelectGraph: a replay after writing new values into the static inputs gives
+    what the eager block_select gives on those values (decode-shaped batch)."""
+    from unum_ops_b200 import BlockSelectGraph, block_select
+
+    rng = np.random.default_rng(31)
+    B = 24
+    ctx = rng.integers(300, 9000, size=B)
+    k_lens = (ctx - 32) // 16 + 1
+    q = torch.randn(B, 32, 128, device=dev).to(torch.bfloat16)
+    k = torch.randn(int(k_lens.sum()), 2, 128, device=dev).to(torch.bfloat16)
+    cu_q = torch.arange(B + 1, dtype=torch.int32, device=dev)
+    cu_k = _t(cases.cu(k_lens), dev)
+    table = _t(rng.integers(0, 1 << 20, size=(B, 256)).astype(np.int32), dev)
+    tb = torch.arange(B, dtype=torch.int32, device=dev)
+    pos = _t(ctx.astype(np.int32), dev)
+    cache = _t((ctx - 1).astype(np.int32), dev)
+    args = (q, k, cu_q, cu_k, int(k_lens.max()), table, tb, pos, pos)
+    kw = dict(max_context_len=16384, cache_lens=cache)
+    gr = BlockSelectGraph(*args, **kw)
+    for _ in range(2):
+        q.copy_(torch.randn_like(q, dtype=torch.float32).to(torch.bfloat16))
+        k.copy_(torch.randn_like(k, dtype=torch.float32).to(torch.bfloat16))
+        got = [x.clone() for x in gr()]
+        ref = block_select(*args, **kw)
+        for a, b in zip(got, ref):
+            assert torch.equal(a, b)

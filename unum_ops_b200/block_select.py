@@ -15,7 +15,7 @@ from . import _lib
 from .infllm_v2 import _as_i32, _round_multiple, _workspace, infllmv2_attn_stage1, max_pooling_1d_varlen
 from .sparse_kernel_extension import get_block_table_ref_torch
 
-__all__ = ["topk_blocks", "block_select", "block_select_rows", "block_select_streamed",
+__all__ = ["topk_blocks", "block_select", "BlockSelectGraph", "block_select_rows", "block_select_streamed",
            "get_block_table_shard", "stage1_pooled"]
 
 
@@ -319,3 +319,37 @@ def block_select_streamed(q_host, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_
     if result_host is not None:
         comp.wait_stream(back)
     return scores, pooled, idx, slots
+
+
+class BlockSelectGraph:
+    """``block_select`` captured once in a CUDA graph and replayed per step.
+
+    For decode loops, where one step's kernels run for tens of microseconds and the
+    host-side launch work of the eager call would dominate.  The tensors passed here
+    are the graph's static inputs: write the next step's values into them in place
+    (same shapes, same devices) and call the object; it returns the same
+    (scores, pooled, topk_idx, slots) tensors every time, overwritten by the replay.
+    Keyword arguments are those of ``block_select``.  The capture runs the path
+    three times on a side stream first (allocations, tensor-map setup), as CUDA
+    graph capture requires.
+    """
+
+    def __init__(self, q, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_k, block_table, token_to_bs,
+                 token_pos_in_bs, seqlen_q, **kwargs):
+        dev = _lib.require_cuda(q, k_cmp, cu_seqlens_q, cu_seqlens_k, block_table, token_to_bs)
+        args = (q, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_k, block_table, token_to_bs,
+                token_pos_in_bs, seqlen_q)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                block_select(*args, **kwargs)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.outputs = block_select(*args, **kwargs)
+
+    def __call__(self):
+        self.graph.replay()
+        return self.outputs
