@@ -223,16 +223,20 @@ def make_inputs(seed, device):
 # compressed key of stage 1 (both per kv head), from the kernel times at 128k:
 # stage 1 ~1.0e-11 s per key, top-k + block table ~5.6e-9 s per (token, head).
 TOKEN_COST = 560.0
+# End to end the query rows cross PCIe first: one token's 16 query heads (4 KB) take
+# ~1e-7 s at ~40 GB/s per GPU, ~1e4 visible keys of stage-1 time, so the end-to-end
+# shards are near-equal token ranges (compute, smaller, is hidden under the copies).
+E2E_TOKEN_COST = 1.0e4
 
 
-def shard_of(world, rank, strong):
+def shard_of(world, rank, strong, token_cost=TOKEN_COST):
     """(first kv head, kv heads, t_begin, t_end) this rank computes: config 3's kv head x
     query range shard with strong scaling, the whole sequence with weak scaling."""
     from unum_ops_b200.sharding import prefill_shard
 
     if world == 1 or not strong:
         return 0, HK, 0, L_SEQ
-    return prefill_shard(world, rank, L_SEQ, NKC, HK, token_cost=TOKEN_COST)
+    return prefill_shard(world, rank, L_SEQ, NKC, HK, token_cost=token_cost)
 
 
 def run_ours(args):
@@ -274,11 +278,22 @@ def run_ours(args):
     idx = torch.empty(nh, nrows, TOPK, dtype=torch.int32, device=dev)
     slots = torch.empty(nrows, nh, TOPK * 64, dtype=torch.int32, device=dev)
     ws = _workspace(dev, int(L.unum_stage1_workspace_size(1)))
-    # topk_idx of all ranks in one place: padded to the longest range
+    # topk_idx of all ranks in one place: every rank's exact shard sent straight into
+    # each rank's full [Hk, T, K] buffer (NCCL point-to-point, no padding)
     ranges = [shard_of(world, r, strong) for r in range(world)]
-    pad_rows = max(r[3] - r[2] for r in ranges)
-    gather_src = torch.zeros(nh, pad_rows, TOPK, dtype=torch.int32, device=dev)
-    gather_dst = torch.empty(world, nh, pad_rows, TOPK, dtype=torch.int32, device=dev)
+    full_idx = torch.empty(HK, L_SEQ, TOPK, dtype=torch.int32, device=dev)
+
+    def gather_idx(local_idx, shards):
+        g, nh_, a, b = shards[rank]
+        full_idx[g:g + nh_, a:b].copy_(local_idx)
+        ops = []
+        for r, (gr, nhr, ar, br) in enumerate(shards):
+            if r == rank:
+                continue
+            ops.append(dist.P2POp(dist.isend, local_idx, r))
+            ops.append(dist.P2POp(dist.irecv, full_idx[gr:gr + nhr, ar:br], r))
+        for w in dist.batch_isend_irecv(ops):
+            w.wait()
 
     def step(ev=None):
         """One block-selection pass over this rank's shard: stage 1 with the pooling
@@ -308,8 +323,7 @@ def run_ours(args):
         if ev is not None:
             ev[3].record(stream)
         if world > 1:
-            gather_src[:, :nrows].copy_(idx)
-            dist.all_gather_into_tensor(gather_dst, gather_src)
+            gather_idx(idx, ranges)
         if ev is not None:
             ev[4].record(stream)
 
@@ -370,21 +384,23 @@ def run_ours(args):
 
     # ---- end to end through the public API with host buffers (pinned), copies timed:
     # this rank's query rows of its kv heads stream in, its top-k ids go back to the host
-    q_pin = host["q"][ta:tb_, g0 * G:(g0 + nh) * G].contiguous().pin_memory()
+    # (end to end the shards balance the host-to-device copy: near-equal token ranges)
+    eg0, enh, ea, eb = shard_of(world, rank, strong, E2E_TOKEN_COST)
+    q_pin = host["q"][ea:eb, eg0 * G:(eg0 + enh) * G].contiguous().pin_memory()
     pin = {k: v.pin_memory() for k, v in host.items() if k != "q"}
-    res_host = torch.empty(nh, nrows, TOPK, dtype=torch.int32).pin_memory()
+    res_host = torch.empty(enh, eb - ea, TOPK, dtype=torch.int32).pin_memory()
 
     def e2e_step():
         """Through the public streamed API: host-resident queries copied in chunk by chunk
         while the previous chunk computes; the top-k ids come back to pinned host memory."""
-        kk = pin["k"][:, g0:g0 + nh].to(dev, non_blocking=True)
+        kk = pin["k"][:, eg0:eg0 + enh].to(dev, non_blocking=True)
         small = {n: pin[n].to(dev, non_blocking=True) for n in ("cu_q", "cu_k", "table", "tb", "pos",
                                                                  "seqlen")}
         block_select_streamed(
             q_pin, kk, small["cu_q"], small["cu_k"], NKC, small["table"], small["tb"],
             small["pos"], small["seqlen"], max_context_len=L_SEQ, init_blocks=INIT_BLOCKS,
             local_blocks=LOCAL_BLOCKS, topk=TOPK, chunk_tokens=16384, result_host=res_host,
-            t_begin=ta, head_offset=g0)
+            t_begin=ea, head_offset=eg0)
 
     e2e_step()
     barrier()
@@ -400,7 +416,7 @@ def run_ours(args):
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    h2d = q_pin.numel() * 2 + pin["k"][:, g0:g0 + nh].numel() * 2 + sum(
+    h2d = q_pin.numel() * 2 + pin["k"][:, eg0:eg0 + enh].numel() * 2 + sum(
         pin[n].numel() * pin[n].element_size() for n in ("cu_q", "cu_k", "table", "tb", "pos", "seqlen"))
     d2h = res_host.numel() * 4
     if world > 1:  # whole-job bytes: every rank's copies
@@ -425,7 +441,8 @@ def run_ours(args):
             gbs = ab[kname] / (mean[kname] * 1e-3) / 1e9
             kernels[kname] = {"ms": mean[kname], "gbs": gbs, "frac": gbs / hbm, "bound": "hbm"}
         if world > 1:
-            kernels["topk_idx_all_gather"] = {"ms": mean["gather"], "bytes": gather_dst.numel() * 4}
+            kernels["topk_idx_gather"] = {"ms": mean["gather"], "bytes": full_idx.numel() * 4,
+                                          "how": "NCCL send/recv of each rank's exact shard"}
         cpu = None
         if args.cpu_sample > 0 and world == 1:
             hf = {k: v.numpy() for k, v in host.items() if k not in ("q", "k")}
@@ -467,7 +484,9 @@ def run_ours(args):
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                     "result": "top-64 block ids int32 of every rank's shard copied to host",
                     "api": "block_select_streamed (query chunks of 16384 tokens copied while the "
-                           "previous chunk computes)"},
+                           "previous chunk computes)",
+                    "shards": "kv head x query range, ranges of near-equal host-to-device bytes"
+                              if strong and world > 1 else "as the device step"},
             "gpu_launches": (2 + (1 if nrows == L_SEQ else nh)) * args.steps,
             "clocks": clocks,
         }
