@@ -15,12 +15,12 @@
 // together.  Table reads are 16-byte vector loads whenever the four positions
 // are valid and inside the row.
 #include "common.cuh"
+#include "gbt_row.cuh"
 
 namespace {
 
-constexpr int kBlock = 64;   // kSparseBlockSize (get_table_torch.py:13)
+constexpr int kBlock = unum::kGbtBlock;
 constexpr int kWarps = 8;
-constexpr int kUnroll = 4;
 
 __global__ void __launch_bounds__(kWarps * 32)
 get_block_table_kernel(const int32_t *__restrict__ topk, int64_t H, int64_t T, int64_t K,
@@ -33,8 +33,6 @@ get_block_table_kernel(const int32_t *__restrict__ topk, int64_t H, int64_t T, i
     const int lane = threadIdx.x & 31;
     const int64_t rows = T * H;
     const int32_t items = (int32_t)(K * (kBlock / 4));  // int4 items per row
-    const int32_t q4 = (lane & 15) * 4;                  // first of this lane's 4 positions in a block
-    const int32_t Lm1 = (int32_t)(L - 1);
     for (int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); row < rows;
          row += (int64_t)gridDim.x * kWarps) {
         const int64_t t = row / H;
@@ -48,42 +46,7 @@ get_block_table_kernel(const int32_t *__restrict__ topk, int64_t H, int64_t T, i
         const int32_t *trow = table + (bs_ok ? (int64_t)bs * bt_stride : 0);
         const int32_t *tk = topk + (int64_t)hl * ts_h + t * ts_t;
         int4 *orow = reinterpret_cast<int4 *>(out + t * out_ts) + (int64_t)hl * items;
-        for (int32_t e0 = 0; e0 < items; e0 += 32 * kUnroll) {
-            int32_t p0[kUnroll];
-#pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
-                const int32_t e = e0 + u * 32 + lane;
-                const int32_t idx = e < items ? __ldg(tk + (int64_t)(e >> 4) * ts_k) : -1;
-                p0[u] = (int32_t)((uint32_t)idx * (uint32_t)kBlock + (uint32_t)q4);
-            }
-            int4 v[kUnroll];
-#pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
-                const int32_t p = p0[u];
-                if (vec_ok && p >= 0 && p <= INT32_MAX - 3 && p + 3 < lim && p + 3 <= Lm1) {
-                    const int4 tv = __ldg(reinterpret_cast<const int4 *>(trow + p));
-                    v[u].x = (int32_t)(head_group * (uint32_t)tv.x + h);
-                    v[u].y = (int32_t)(head_group * (uint32_t)tv.y + h);
-                    v[u].z = (int32_t)(head_group * (uint32_t)tv.z + h);
-                    v[u].w = (int32_t)(head_group * (uint32_t)tv.w + h);
-                } else {
-                    int32_t r[4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int32_t pi = (int32_t)((uint32_t)p + (uint32_t)i);
-                        const bool valid = pi >= 0 && pi < lim;
-                        const int32_t sp = pi < 0 ? 0 : (pi > Lm1 ? Lm1 : pi);  // clamp (get_table_torch.py:35)
-                        r[i] = valid ? (int32_t)(head_group * (uint32_t)__ldg(trow + sp) + h) : 0;
-                    }
-                    v[u] = make_int4(r[0], r[1], r[2], r[3]);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
-                const int32_t e = e0 + u * 32 + lane;
-                if (e < items) __stcs(orow + e, v[u]);
-            }
-        }
+        unum::gbt_emit_row(tk, ts_k, (int32_t)K, trow, lim, (int32_t)L, head_group, h, vec_ok, orow, lane);
     }
 }
 

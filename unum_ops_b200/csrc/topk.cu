@@ -30,6 +30,16 @@ namespace {
 constexpr int kWarps = 4;
 constexpr int kMaxNB = 4096;
 constexpr int kMaxK = 1024;
+#ifndef UNUM_TOPK_CAND
+#define UNUM_TOPK_CAND 640
+#endif
+constexpr int kCandCap = UNUM_TOPK_CAND;  // candidate buffer per warp (a multiple of 32)
+#ifndef UNUM_TOPK_SHRINK
+#define UNUM_TOPK_SHRINK 4  // 16-bit path: narrow the margin once more than 1/4 of the slots fill
+#endif
+#ifndef UNUM_TOPK_MINBLOCKS
+#define UNUM_TOPK_MINBLOCKS 7
+#endif
 
 template <typename T> __device__ __forceinline__ float to_f(T v);
 template <> __device__ __forceinline__ float to_f<float>(float v) { return v; }
@@ -105,10 +115,10 @@ __device__ __forceinline__ void load8(const Key *keys, int32_t i0, uint32_t (&k)
     }
 }
 
-// Candidate keys (512 slots) or, on the 16-bit path, three bitmaps over block ids.
+// Candidate keys (kCandCap slots) or, on the 16-bit path, three bitmaps over block ids.
 template <typename Key>
 __host__ __device__ constexpr size_t cand_region_bytes(size_t nbp) {
-    return 512 * sizeof(Key) > 12 * nbp / 32 ? 512 * sizeof(Key) : 12 * nbp / 32;
+    return kCandCap * sizeof(Key) > 12 * nbp / 32 ? kCandCap * sizeof(Key) : 12 * nbp / 32;
 }
 
 // Shared memory of one warp: histogram, staged keys (16-bit path: the row's raw
@@ -117,7 +127,7 @@ __host__ __device__ constexpr size_t cand_region_bytes(size_t nbp) {
 template <typename Key>
 __host__ __device__ constexpr size_t warp_smem_bytes(int64_t NB) {
     const size_t nbp = (size_t)((NB + 255) / 256 * 256);
-    return 1024 + nbp * sizeof(Key) + cand_region_bytes<Key>(nbp) + 512 * 2;
+    return 1024 + nbp * sizeof(Key) + cand_region_bytes<Key>(nbp) + kCandCap * 2;
 }
 
 // Histogram of the staged keys[0, n_pad) whose bits under pmask equal prefix, by
@@ -334,7 +344,6 @@ __device__ __forceinline__ void emit_selected(const Key *keys, int32_t n, int32_
     for (int32_t s2 = (pos < K ? pos : K) + lane; s2 < K; s2 += 32) orow[s2] = -1;
 }
 
-constexpr int kCandCap = 512;   // candidate buffer per warp
 // threshold margin in key steps: 32 bf16/fp16 steps (bf16: 2^(32/128) = 19 % in value);
 // the same relative width for 32-bit keys
 template <typename Key> constexpr uint32_t kMargin = sizeof(Key) == 2 ? 32u : (32u << 16);
@@ -385,10 +394,10 @@ __device__ __noinline__ uint4 load8_bits_slow(const T *src, int32_t i0, int32_t 
 // bitmap eqw is ignored (eq_mode 0), replaces the ties (1) or is taken whole (2).
 // Lane l sweeps a contiguous run of words, so ids come out ascending; then -1
 // padding.
+template <int kMaxW>  // bitmap words a lane sweeps at most: NBp / 32 / 32
 __device__ __forceinline__ void emit_bitmap(const uint32_t *selw, const uint32_t *tiew, const uint32_t *eqw,
                                             int eq_mode, int32_t nw, int32_t K, int32_t remaining,
                                             int lane, int32_t *orow) {
-    constexpr int kMaxW = kMaxNB / 32 / 32;  // words a lane sweeps at most
     const int32_t wpl = (nw + 31) >> 5;
     const int32_t w0 = lane * wpl;
     uint32_t sw[kMaxW], tw[kMaxW];
@@ -460,8 +469,8 @@ template <> __device__ __forceinline__ float key_value<float>(uint32_t k) {
 // When the bound misses (no previous row, fewer than K entries above it, or
 // more than the slots hold) the row is staged in shared memory as keys and the
 // full radix select runs on it.  Results never depend on which path ran.
-template <typename T>
-__global__ void __launch_bounds__(kWarps * 32, sizeof(T) == 2 ? 7 : 1)  // 16-bit: 7 blocks, <= 72 registers
+template <typename T, int kMaxW>  // kMaxW: 2 for rows of at most 2048 blocks, else 4
+__global__ void __launch_bounds__(kWarps * 32, sizeof(T) == 2 ? UNUM_TOPK_MINBLOCKS : 1)  // 16-bit: 7 blocks, <= 72 registers
 topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_stride, int32_t K,
             bool vec_ok, int64_t rows_per_warp, int32_t *__restrict__ out) {
     using Key = typename KeyOf<T>::K;
@@ -553,7 +562,7 @@ topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_
                 const bool ovf = __any_sync(0xffffffffu, cnt > (uint32_t)kLaneCand);
                 const bool under = n_st + E < K;  // the threshold lies below t0
                 if (ovf) margin = margin / 2 > kMarginMin ? margin / 2 : kMarginMin;
-                else if (n_st > kCandCap / 4) margin = margin - margin / 4 > kMarginMin ? margin - margin / 4 : kMarginMin;
+                else if (n_st > kCandCap / UNUM_TOPK_SHRINK) margin = margin - margin / 4 > kMarginMin ? margin - margin / 4 : kMarginMin;
                 else if (under && t0 > kMinFinite<T>) margin = margin * 2 < kMarginMax ? margin * 2 : kMarginMax;
                 __syncwarp();
                 if (!ovf && !under) {
@@ -568,7 +577,7 @@ topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_
                         else if (k == prefix) atomicOr(&tiew[id >> 5], 1u << (id & 31));
                     }
                     __syncwarp();
-                    emit_bitmap(selw, tiew, eqw, eq_mode, nw, K, remaining, lane, orow);
+                    emit_bitmap<kMaxW>(selw, tiew, eqw, eq_mode, nw, K, remaining, lane, orow);
                     done = true;
                 }
                 // overflow, or no finite bound left to lower: the staged radix select below
@@ -628,10 +637,12 @@ topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_
                 }
             }
             __syncwarp();
-            if (n > kCandCap) margin = margin / 2 > kMarginMin ? margin / 2 : kMarginMin;
-            else if (n > kCandCap / 2) margin = margin - margin / 4 > kMarginMin ? margin - margin / 4 : kMarginMin;
+            // the radix select pads the candidates to whole 256-key steps: at most kCand32 of them
+            constexpr int32_t kCand32 = kCandCap / 256 * 256;
+            if (n > kCand32) margin = margin / 2 > kMarginMin ? margin / 2 : kMarginMin;
+            else if (n > kCand32 / 2) margin = margin - margin / 4 > kMarginMin ? margin - margin / 4 : kMarginMin;
             else if (n < K && t0 > kMinFinite<T>) margin = margin * 2 < kMarginMax ? margin * 2 : kMarginMax;
-            if (n >= K && n <= kCandCap) {
+            if (n >= K && n <= kCand32) {
                 const int32_t npad = (n + 255) & ~255;
                 for (int32_t i = n + lane; i < npad; i += 32) ckey[i] = Key(0);
                 __syncwarp();
@@ -673,7 +684,8 @@ int launch_topk(const void *scores, int64_t rows, int64_t NB, int64_t row_stride
                 int32_t *out, cudaStream_t s) {
     using Key = typename KeyOf<T>::K;
     const size_t smem = (size_t)kWarps * warp_smem_bytes<Key>(NB);
-    auto kern = topk_kernel<T>;
+    const int64_t NBp = (NB + 255) / 256 * 256;
+    auto kern = NBp <= 2048 ? topk_kernel<T, 2> : topk_kernel<T, kMaxNB / 32 / 32>;
     UNUM_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     // a few long runs of consecutive rows per warp, so most rows reuse a threshold
     const int64_t want = (rows + kWarps - 1) / kWarps;
