@@ -527,7 +527,7 @@ def run_decode(args):
         dist.init_process_group("nccl", device_id=dev)
     unum_ops_b200.load()
     strong = args.scaling == "strong"
-    B_all = 512
+    B_all = args.decode_batch
     seed = 4 + (0 if strong else rank)
     rng = np.random.default_rng(seed)
     ctx_all = rng.integers(4096, 65537, size=B_all)
@@ -601,7 +601,7 @@ def run_decode(args):
         hbm = load_peaks()[0]
         seqs = B_all if strong else world * B_all
         emit({
-            "metric": "decode block selection, sequences/s (512 x 1 query, contexts U[4096,65536])",
+            "metric": f"decode block selection, sequences/s ({B_all} x 1 query, contexts U[4096,65536])",
             "value": seqs / (ms * 1e-3), "unit": "sequences/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong" if strong else "weak",
@@ -713,6 +713,8 @@ def main():
                     help="prefill: the 128k headline (config 3); decode: config 4")
     ap.add_argument("--seqlen", type=int, default=131072,
                     help="prefill length (default: the 128k headline workload)")
+    ap.add_argument("--decode-batch", type=int, default=512,
+                    help="decode workload: sequences in the batch (config 4: 512)")
     ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
                     help="N>1: strong = one sequence sharded by kv head x query range "
                          "(config 3); weak = every rank its own sequence")

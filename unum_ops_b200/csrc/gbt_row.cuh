@@ -17,15 +17,17 @@ constexpr int kGbtBlock = 64;   // kSparseBlockSize (get_table_torch.py:13)
 constexpr int kGbtUnroll = 4;
 
 // tk: the row's K block ids (stride ts_k); trow: the sequence's block-table row
-// (L entries); orow: the row's K*64 output ids (16-byte aligned).
+// (L entries); orow: the row's K*64 output ids (16-byte aligned).  Writes the row's
+// int4 items [e_begin, e_end) (of K*16; e_begin a multiple of 32*kGbtUnroll).
 __device__ __forceinline__ void gbt_emit_row(const int32_t *__restrict__ tk, int64_t ts_k, int32_t K,
                                              const int32_t *__restrict__ trow, int32_t lim, int32_t L,
                                              uint32_t head_group, uint32_t h, bool vec_ok,
-                                             int4 *__restrict__ orow, int lane) {
-    const int32_t items = K * (kGbtBlock / 4);  // int4 items per row
+                                             int4 *__restrict__ orow, int lane, int32_t e_begin,
+                                             int32_t e_end) {
+    const int32_t items = e_end;
     const int32_t q4 = (lane & 15) * 4;         // first of this lane's 4 positions in a block
     const int32_t Lm1 = L - 1;
-    for (int32_t e0 = 0; e0 < items; e0 += 32 * kGbtUnroll) {
+    for (int32_t e0 = e_begin; e0 < items; e0 += 32 * kGbtUnroll) {
         int32_t p0[kGbtUnroll];
 #pragma unroll
         for (int u = 0; u < kGbtUnroll; ++u) {

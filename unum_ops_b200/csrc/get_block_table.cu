@@ -22,19 +22,27 @@ namespace {
 constexpr int kBlock = unum::kGbtBlock;
 constexpr int kWarps = 8;
 
+template <bool kSeg>  // false: one unit per whole row (span = the row)
 __global__ void __launch_bounds__(kWarps * 32)
 get_block_table_kernel(const int32_t *__restrict__ topk, int64_t H, int64_t T, int64_t K,
                        int64_t ts_h, int64_t ts_t, int64_t ts_k,
                        const int32_t *__restrict__ table, int64_t B, int64_t L, int64_t bt_stride,
                        const int32_t *__restrict__ token_to_bs, const int32_t *__restrict__ pos_in_bs,
                        int pos_scalar, const int32_t *__restrict__ seqlen, int seqlen_scalar,
-                       uint32_t head_group, uint32_t h0, int64_t out_ts, bool vec_ok,
+                       uint32_t head_group, uint32_t h0, int64_t out_ts, bool vec_ok, int32_t span,
                        int32_t *__restrict__ out) {
     const int lane = threadIdx.x & 31;
     const int64_t rows = T * H;
     const int32_t items = (int32_t)(K * (kBlock / 4));  // int4 items per row
-    for (int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); row < rows;
-         row += (int64_t)gridDim.x * kWarps) {
+    // work unit = (row, segment of `span` int4 items, a multiple of 128): few rows (decode
+    // batches) still spread over the GPU
+    const int32_t n_seg = kSeg ? (items + span - 1) / span : 1;
+    const int64_t units = rows * n_seg;
+    for (int64_t unit = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); unit < units;
+         unit += (int64_t)gridDim.x * kWarps) {
+        const int64_t row = kSeg ? unit / n_seg : unit;
+        const int32_t eA = kSeg ? (int32_t)(unit - row * n_seg) * span : 0;
+        const int32_t eB = kSeg ? (eA + span < items ? eA + span : items) : items;
         const int64_t t = row / H;
         const uint32_t hl = (uint32_t)(row - t * H);  // head within topk / out
         const uint32_t h = hl + h0;                    // head index in the block-table values
@@ -46,7 +54,8 @@ get_block_table_kernel(const int32_t *__restrict__ topk, int64_t H, int64_t T, i
         const int32_t *trow = table + (bs_ok ? (int64_t)bs * bt_stride : 0);
         const int32_t *tk = topk + (int64_t)hl * ts_h + t * ts_t;
         int4 *orow = reinterpret_cast<int4 *>(out + t * out_ts) + (int64_t)hl * items;
-        unum::gbt_emit_row(tk, ts_k, (int32_t)K, trow, lim, (int32_t)L, head_group, h, vec_ok, orow, lane);
+        unum::gbt_emit_row(tk, ts_k, (int32_t)K, trow, lim, (int32_t)L, head_group, h, vec_ok, orow, lane,
+                           eA, eB);
     }
 }
 
@@ -71,13 +80,22 @@ int launch_gbt(const int32_t *topk_idx, int64_t H, int64_t T, int64_t K, int64_t
                    "out token stride must cover H*K*64 ids and be a multiple of 4");
     const bool vec_ok = unum::aligned16(block_table) && (bt_stride % 4 == 0);
     const int64_t rows = T * H;
-    const int64_t want = (rows + kWarps - 1) / kWarps;
+    // rows split into segments when there are fewer than ~64 warps' worth per SM (decode)
+    const int64_t items = K * (kBlock / 4);
+    const int64_t target = (int64_t)unum::sm_count() * 64;
+    const int64_t ip = (items + 127) / 128;  // 128-item steps per row
+    int64_t n_seg = rows >= target ? 1 : (target + rows - 1) / rows;
+    if (n_seg > ip) n_seg = ip;
+    const int32_t span = (int32_t)((ip + n_seg - 1) / n_seg * 128);
+    const int64_t units = rows * ((items + span - 1) / span);
+    const int64_t want = (units + kWarps - 1) / kWarps;
     const int64_t cap = (int64_t)unum::sm_count() * 32;
     const int grid = (int)(want < cap ? want : cap);
-    get_block_table_kernel<<<grid, kWarps * 32, 0, (cudaStream_t)stream>>>(
+    auto kern = n_seg > 1 ? get_block_table_kernel<true> : get_block_table_kernel<false>;
+    kern<<<grid, kWarps * 32, 0, (cudaStream_t)stream>>>(
         topk_idx, H, T, K, ts_h, ts_t, ts_k, block_table, B, L, bt_stride, token_to_bs,
         token_pos_in_bs, pos_is_scalar, seqlen_q, seqlen_is_scalar, (uint32_t)head_group,
-        (uint32_t)h0, out_ts, vec_ok, out);
+        (uint32_t)h0, out_ts, vec_ok, span, out);
     return unum::check_launch("get_block_table_kernel");
 }
 }  // namespace

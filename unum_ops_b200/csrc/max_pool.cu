@@ -71,7 +71,7 @@ max_pool_kernel(const T *__restrict__ in, int64_t numel, int64_t H, int64_t T_, 
                 const int32_t *__restrict__ cu_q, const int32_t *__restrict__ cu_k,
                 const int32_t *__restrict__ cache_lens, int64_t n_seq, int64_t NB, int64_t sp,
                 int64_t block_size, int64_t init_blocks, int64_t local_blocks, bool vec_ok,
-                T *__restrict__ out) {
+                int32_t span, T *__restrict__ out) {
     constexpr int VEC = 16 / sizeof(T);  // scores per 16-byte load
     constexpr int OPV = VEC / 4;         // pooled outputs per load when sp == 4
     const int lane = threadIdx.x & 31;
@@ -79,8 +79,15 @@ max_pool_kernel(const T *__restrict__ in, int64_t numel, int64_t H, int64_t T_, 
     const int64_t ksize = sp + 1;
     const int32_t nb = (int32_t)NB;
     const bool pair_ok = (NB % 2) == 0;  // 2 outputs per lane per vector: aligned word stores
-    for (int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); row < rows;
-         row += (int64_t)gridDim.x * kWarps) {
+    // work unit = (row, segment of `span` output blocks; span a multiple of 128, so the
+    // 16-byte chunks of a segment never straddle its ends): few rows still fill the GPU
+    const int32_t n_seg = (nb + span - 1) / span;
+    const int64_t units = rows * n_seg;
+    for (int64_t unit = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); unit < units;
+         unit += (int64_t)gridDim.x * kWarps) {
+        const int64_t row = unit / n_seg;
+        const int32_t jA = (int32_t)(unit - row * n_seg) * span;
+        const int32_t jB = jA + span < nb ? jA + span : nb;
         const int64_t h = row / T_, t = row - h * T_;
         const int b = find_seq(cu_q, n_seq, t);
         int32_t k_len = 0, off_bq = 0;
@@ -99,12 +106,15 @@ max_pool_kernel(const T *__restrict__ in, int64_t numel, int64_t H, int64_t T_, 
         int32_t j_end = k_len > 0 ? (int32_t)((k_len + sp) / sp) : 0;
         if (j_end > nb) j_end = nb;
         auto masked = [&](int32_t j) { return j < init_b || (off_bq >= j && off_bq <= j + local_b); };
-        int32_t j_done = 0;
-        if (vec_ok && sp == 4 && OPV == 2) {
+        int32_t j_done = jA;
+        // score 4*jA-1, the left end of the segment's first window
+        const float carry0 = (jA > 0 && 4 * jA - 1 < avail) ? to_f<T>(src[4 * jA - 1]) : -INFINITY;
+        const int32_t jE = j_end < jB ? j_end : jB;  // vector paths: blocks [jA, jE)
+        if (vec_ok && sp == 4 && OPV == 2 && jE > jA) {
             // 16-bit scores: a 16-byte vector = 8 scores = the windows of 2 blocks
-            const int32_t n_chunks = (j_end + 1) / 2;
-            float carry = -INFINITY;  // score 8c-1 for lane 0 of the next step
-            for (int32_t c0 = 0; c0 < n_chunks; c0 += 64) {
+            const int32_t n_chunks = (jE + 1) / 2;
+            float carry = carry0;  // score 8c-1 for lane 0 of the next step
+            for (int32_t c0 = jA / 2; c0 < n_chunks; c0 += 64) {
                 float e[2][8];
 #pragma unroll
                 for (int u = 0; u < 2; ++u) {
@@ -133,7 +143,7 @@ max_pool_kernel(const T *__restrict__ in, int64_t numel, int64_t H, int64_t T_, 
                                          fmaxf(fmaxf(e[u][1], e[u][2]), e[u][3]));
                         float m1 = fmaxf(fmaxf(e[u][3], e[u][4]), fmaxf(fmaxf(e[u][5], e[u][6]), e[u][7]));
                         m0 = masked(j) ? INFINITY : m0;          // j < j_end: window non-empty
-                        if (j + 1 < j_end) {
+                        if (j + 1 < jE) {
                             m1 = masked(j + 1) ? INFINITY : m1;
                             store2<T>(orow + j, m0, m1, pair_ok);
                         } else {
@@ -142,34 +152,34 @@ max_pool_kernel(const T *__restrict__ in, int64_t numel, int64_t H, int64_t T_, 
                     }
                 }
             }
-            j_done = j_end;
-        } else if (vec_ok && sp == 4) {
+            j_done = jE;
+        } else if (vec_ok && sp == 4 && jE > jA) {
             // fp32 scores: a 16-byte vector = 4 scores = the window of 1 block
-            float carry = -INFINITY;
-            for (int32_t c0 = 0; c0 < j_end; c0 += 32) {
+            float carry = carry0;
+            for (int32_t c0 = jA; c0 < jE; c0 += 32) {
                 const int32_t c = c0 + lane;
                 const int32_t p0 = c * 4;
                 float e[4];
-                if (c < j_end && p0 + 4 <= avail) {
+                if (c < jE && p0 + 4 <= avail) {
                     const float4 v = __ldg(reinterpret_cast<const float4 *>(src + p0));
                     e[0] = v.x; e[1] = v.y; e[2] = v.z; e[3] = v.w;
                 } else {
 #pragma unroll
                     for (int i = 0; i < 4; ++i)
-                        e[i] = (c < j_end && p0 + i < avail) ? to_f<T>(src[p0 + i]) : -INFINITY;
+                        e[i] = (c < jE && p0 + i < avail) ? to_f<T>(src[p0 + i]) : -INFINITY;
                 }
                 float prev = __shfl_up_sync(0xffffffffu, e[3], 1);
                 if (lane == 0) prev = carry;
                 carry = __shfl_sync(0xffffffffu, e[3], 31);
-                if (c < j_end) {
+                if (c < jE) {
                     float m = fmaxf(fmaxf(c == 0 ? -INFINITY : prev, e[0]), fmaxf(fmaxf(e[1], e[2]), e[3]));
                     orow[c] = from_f<T>(masked(c) ? INFINITY : m);
                 }
             }
-            j_done = j_end;
+            j_done = jE;
         }
-        // scalar path (general layouts) and the empty-window tail
-        for (int32_t j = j_done + lane; j < nb; j += 32) {
+        // scalar path (general layouts) and the empty-window tail of the segment
+        for (int32_t j = j_done + lane; j < jB; j += 32) {
             const int64_t ws = (int64_t)j * sp - 1;
             float mx = -INFINITY;
             for (int64_t ki = 0; ki < ksize; ++ki) {
@@ -205,7 +215,14 @@ extern "C" int unum_max_pooling_1d_varlen(const void *input, int dtype, int64_t 
                    "null pointer argument");
     const int64_t fs = max_seqlen_q / stride;
     const int64_t rows = H * T;
-    const int64_t want = (rows + kWarps - 1) / kWarps;
+    // rows split into segments when there are fewer than ~64 warps' worth per SM (decode)
+    const int64_t target = (int64_t)unum::sm_count() * 64;
+    const int64_t nbp = (NB + 127) / 128 * 128;
+    int64_t n_seg = rows >= target ? 1 : (target + rows - 1) / rows;
+    if (n_seg > nbp / 128) n_seg = nbp / 128;
+    const int32_t span = (int32_t)((nbp / 128 + n_seg - 1) / n_seg * 128);
+    const int64_t units = rows * ((NB + span - 1) / span);
+    const int64_t want = (units + kWarps - 1) / kWarps;
     const int64_t cap = (int64_t)unum::sm_count() * 32;
     const int grid = (int)(want < cap ? want : cap);
     cudaStream_t s = (cudaStream_t)stream;
@@ -215,18 +232,18 @@ extern "C" int unum_max_pooling_1d_varlen(const void *input, int dtype, int64_t 
         case UNUM_DTYPE_F32:
             max_pool_kernel<float><<<grid, kWarps * 32, 0, s>>>(
                 (const float *)input, input_numel, H, T, fs, cu_seqlens_q, cu_seqlens_k, cache_lens,
-                n_seq, NB, sp, block_size, init_blocks, local_blocks, vec_ok, (float *)out);
+                n_seq, NB, sp, block_size, init_blocks, local_blocks, vec_ok, span, (float *)out);
             break;
         case UNUM_DTYPE_BF16:
             max_pool_kernel<__nv_bfloat16><<<grid, kWarps * 32, 0, s>>>(
                 (const __nv_bfloat16 *)input, input_numel, H, T, fs, cu_seqlens_q, cu_seqlens_k,
-                cache_lens, n_seq, NB, sp, block_size, init_blocks, local_blocks, vec_ok,
+                cache_lens, n_seq, NB, sp, block_size, init_blocks, local_blocks, vec_ok, span,
                 (__nv_bfloat16 *)out);
             break;
         case UNUM_DTYPE_F16:
             max_pool_kernel<__half><<<grid, kWarps * 32, 0, s>>>(
                 (const __half *)input, input_numel, H, T, fs, cu_seqlens_q, cu_seqlens_k,
-                cache_lens, n_seq, NB, sp, block_size, init_blocks, local_blocks, vec_ok,
+                cache_lens, n_seq, NB, sp, block_size, init_blocks, local_blocks, vec_ok, span,
                 (__half *)out);
             break;
         default:
