@@ -863,12 +863,17 @@ int launch_main(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap 
 // the compressed keys.  TMEM is a ring of 512/G tile slots released tile by
 // tile, so consecutive items overlap.  Items are taken from a work counter (workspace word 1,
 // zeroed by the prologue), so CTAs stay balanced although items differ in size.
-constexpr int kDecStages = 4;        // K ring depth
+#ifndef UNUM_DEC_STAGES
+#define UNUM_DEC_STAGES 4
+#endif
+constexpr int kDecStages = UNUM_DEC_STAGES;  // K ring depth
 constexpr int kDecSlots = 4;         // item queue depth (an item = its id + its q tile)
-constexpr int kDecEpiWarps = 4;      // 128 epilogue threads = TMEM lanes = keys of a tile
-constexpr int kDecProducerWarp = 4;
-constexpr int kDecMmaWarp = 5;
-constexpr int kDecThreads = 6 * 32;
+// 8 epilogue warps: warps w and w+4 read TMEM lane quarter w%4 (keys 32*(w%4)..+31 of a
+// tile) and take alternate batches of tiles, so each scheduler has two of them
+constexpr int kDecEpiWarps = 8;
+constexpr int kDecProducerWarp = 8;
+constexpr int kDecMmaWarp = 9;
+constexpr int kDecThreads = 10 * 32;
 constexpr int kDecEpiBarrier = 1;
 constexpr uint32_t kDecQSlot = 2 * 32 * 128;                 // two 64-column panels of up to 32 heads
 constexpr uint32_t kDecOffK = kDecSlots * kDecQSlot;          // 32 KB
@@ -1023,7 +1028,7 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
             mbar_init(k_empty + 8 * i, 1);
         }
         for (int i = 0; i < kDecSlots; ++i) mbar_init(tmem_full + 8 * i, 1);
-        for (uint32_t i = 0; i < kTs; ++i) mbar_init(slot_empty + 8 * i, kDecEpiWarps);
+        for (uint32_t i = 0; i < kTs; ++i) mbar_init(slot_empty + 8 * i, 4);  // a tile's 4 reader warps
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -1116,8 +1121,10 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
         // ------------------------------------------------------------ epilogue
         // thread tid = TMEM lane = key tid of every tile; tile kt of an item sits in ring slot
         // (tbase + kt) % kTs, columns slot*G..
-        const int tid = threadIdx.x;  // 0..127
-        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        const int tid = threadIdx.x;    // 0..255
+        const int key = tid & 127;      // TMEM lane = key within a tile
+        const int par = warp >> 2;      // which batches of tiles this warp reads
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
         const float c = p.c;
         uint32_t tbase = 0;  // TMEM tiles consumed
         for (uint32_t n = 0;; ++n) {
@@ -1134,46 +1141,62 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                 const bool bad2 = !wait_bar(sy, tmem_full + 8 * s, (n / kDecSlots) & 1, 18);
                 if (named_bar_or(kDecEpiBarrier, kDecEpiWarps * 32, bad2)) break;
                 tc_fence_after();
-                float v[G], m[G], l[G];
+                // TMEM reads in batches of kTB tiles (64 columns) per wait
+                constexpr int kTB = 64 / G;
+                float vb[kTB][G], m[G], l[G];
+                auto load_batch = [&](int32_t kt0) {
+#pragma unroll
+                    for (int b = 0; b < kTB; ++b)
+                        if (kt0 + b < it.nkt)
+                            tmem_ld_cols<G>(tmem + lane_base + ((tbase + kt0 + b) % kTs) * G, vb[b]);
+                    tmem_wait_ld();
+                };
 #pragma unroll
                 for (int i = 0; i < G; ++i) m[i] = -INFINITY;
-                for (int32_t kt = 0; kt < it.nkt; ++kt) {
-                    tmem_ld_cols<G>(tmem + lane_base + ((tbase + kt) % kTs) * G, v);
-                    tmem_wait_ld();
-                    if (kt * kBN + tid < it.vis) {
+                for (int32_t kt0 = par * kTB; kt0 < it.nkt; kt0 += 2 * kTB) {
+                    load_batch(kt0);
 #pragma unroll
-                        for (int i = 0; i < G; ++i) m[i] = fmaxf(m[i], v[i]);
+                    for (int b = 0; b < kTB; ++b) {
+                        if ((kt0 + b) * kBN + key < it.vis) {
+#pragma unroll
+                            for (int i = 0; i < G; ++i) m[i] = fmaxf(m[i], vb[b][i]);
+                        }
                     }
                 }
                 dec_reduce<G, true>(m, red, warp, lane);
 #pragma unroll
                 for (int i = 0; i < G; ++i) l[i] = 0.f;
-                for (int32_t kt = 0; kt < it.nkt; ++kt) {
-                    tmem_ld_cols<G>(tmem + lane_base + ((tbase + kt) % kTs) * G, v);
-                    tmem_wait_ld();
-                    if (kt * kBN + tid < it.vis) {
+                for (int32_t kt0 = par * kTB; kt0 < it.nkt; kt0 += 2 * kTB) {
+                    load_batch(kt0);
 #pragma unroll
-                        for (int i = 0; i < G; ++i) l[i] += ex2((v[i] - m[i]) * c);
+                    for (int b = 0; b < kTB; ++b) {
+                        if ((kt0 + b) * kBN + key < it.vis) {
+#pragma unroll
+                            for (int i = 0; i < G; ++i) l[i] += ex2((vb[b][i] - m[i]) * c);
+                        }
                     }
                 }
                 dec_reduce<G, false>(l, red + kDecEpiWarps * 32, warp, lane);
 #pragma unroll
                 for (int i = 0; i < G; ++i) m[i] = fmaf(m[i], c, log2f(l[i]));  // b = m*c + log2(l)
-                for (int32_t kt = 0; kt < it.nkt; ++kt) {
-                    tmem_ld_cols<G>(tmem + lane_base + ((tbase + kt) % kTs) * G, v);
-                    tmem_wait_ld();
-                    // this warp's last read of the tile: its slot may take a new tile
+                for (int32_t kt0 = par * kTB; kt0 < it.nkt; kt0 += 2 * kTB) {
+                    load_batch(kt0);
+                    // this warp's last read of these tiles: their slots may take new tiles
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(slot_empty + 8 * ((tbase + kt) % kTs));
-                    const int32_t j = kt * kBN + tid;
-                    float o = 0.f;
-                    if (j < it.vis) {
+                    if (lane < kTB && kt0 + lane < it.nkt) mbar_arrive(slot_empty + 8 * ((tbase + kt0 + lane) % kTs));
 #pragma unroll
-                        for (int i = 0; i < G; ++i) o += ex2(fmaf(v[i], c, -m[i]));
-                        o = fmaxf(o, 0.f);  // NaN scores give 0, as in the tile kernel
+                    for (int b = 0; b < kTB; ++b) {
+                        const int32_t j = (kt0 + b) * kBN + key;
+                        if (kt0 + b >= it.nkt) break;
+                        float o = 0.f;
+                        if (j < it.vis) {
+#pragma unroll
+                            for (int i = 0; i < G; ++i) o += ex2(fmaf(vb[b][i], c, -m[i]));
+                            o = fmaxf(o, 0.f);  // NaN scores give 0, as in the tile kernel
+                        }
+                        if (j < p.out_stride) orow[j] = __float2bfloat16_rn(o);
                     }
-                    if (j < p.out_stride) orow[j] = __float2bfloat16_rn(o);
                 }
                 named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);  // every thread has read item_id[s]
                 tbase += (uint32_t)it.nkt;
