@@ -274,6 +274,11 @@ def block_select_streamed(q_host, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_
     # causal masking the late tokens cost the most, so the cheapest chunk is the one
     # left exposed after the final copy
     cuts = [t_begin] + list(range((t_begin // step + 1) * step, t_end, step)) + [t_end]
+    # the chunk processed last (the window's first) is split once more, so the compute and
+    # the id copy-back left after the final host-to-device copy are short
+    tail = max(step // 4 // 128 * 128, 128)
+    if len(cuts) > 2 and cuts[1] - cuts[0] > 2 * tail:
+        cuts.insert(1, cuts[0] + tail)
     bounds = [(cuts[i], cuts[i + 1]) for i in range(len(cuts) - 1)][::-1]
     copied = []
     # the query buffer may reuse memory that kernels of an earlier call on the compute
