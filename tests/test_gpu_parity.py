@@ -534,3 +534,34 @@ def test_block_select_graph_replays_new_inputs(dev):
         ref = block_select(*args, **kw)
         for a, b in zip(got, ref):
             assert torch.equal(a, b)
+
+
+def test_decode_kernel_token_windows_equal_full(dev):
+    """Stage 1 on token windows of a decode batch (the decode kernel's t_begin/t_end
+    path: the window entry point without fused pooling) writes exactly the window's
+    rows, equal to the same rows of the whole-batch call."""
+    from unum_ops_b200 import _lib
+    from unum_ops_b200.infllm_v2 import _workspace, infllmv2_attn_stage1, stage1_status
+
+    rng = np.random.default_rng(51)
+    B = 40
+    ctx = rng.integers(200, 8000, size=B)
+    k_lens = (ctx - 32) // 16 + 1
+    q = torch.randn(B, 32, 128, device=dev).to(torch.bfloat16)
+    k = torch.randn(int(k_lens.sum()), 2, 128, device=dev).to(torch.bfloat16)
+    cu_q = torch.arange(B + 1, dtype=torch.int32, device=dev)
+    cu_k = _t(cases.cu(k_lens), dev)
+    full = infllmv2_attn_stage1(q, k, None, cu_q, cu_k, max_seqlen_k=int(k_lens.max()), causal=True)
+    W = full.shape[-1]
+    out = torch.full_like(full, float("nan"))
+    L = _lib.load()
+    ws = _workspace(dev, int(L.unum_stage1_workspace_size(B)))
+    for a, b in ((0, 13), (13, 14), (14, 40)):
+        _lib.check(L.unum_infllmv2_attn_stage1_window(
+            q.data_ptr(), B, 32, 128, q.stride(0), q.stride(1), k.data_ptr(), k.shape[0], 2, k.stride(0),
+            k.stride(1), cu_q.data_ptr(), cu_k.data_ptr(), B, 128 ** -0.5, 1, out.data_ptr(), W, None, 0,
+            0, 0, a, b, ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev)))
+        torch.cuda.synchronize()
+        assert stage1_status(dev) == 0
+        assert torch.equal(out[:, a:b], full[:, a:b])
+        assert torch.isnan(out[:, b:].float()).all()  # rows past the window untouched
