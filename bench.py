@@ -381,6 +381,36 @@ def run_ours(args):
             api["pool"].append(a1.elapsed_time(a2))
             del sc
     del scores, pooled, slots
+    producer = None
+    if world == 1:
+        # context: the producer of k_cmp — mean-pool the sequence's keys over 32-token
+        # windows at stride 16 (k [131072, 2, 128] bf16 -> k_cmp [8191, 2, 128])
+        from unum_ops_b200 import compress_keys
+
+        gk = torch.Generator(device=dev).manual_seed(99)
+        k_full = torch.randn(L_SEQ, HK, D, generator=gk, device=dev).to(torch.bfloat16)
+        cu_full = torch.tensor([0, L_SEQ], dtype=torch.int32, device=dev)
+        cu_host = cu_full.cpu()
+        kc, cu_out = compress_keys(k_full, cu_full, cu_seqlens_host=cu_host)
+
+        def produce():  # the kernel alone: sizes precomputed, as a decode loop would hold them
+            unum_ops_b200._lib.check(L.unum_compress_keys(
+                k_full.data_ptr(), L_SEQ, HK, D, k_full.stride(0), k_full.stride(1), cu_full.data_ptr(),
+                cu_out.data_ptr(), 1, kc.shape[0], 32, 16, kc.data_ptr(), stream.cuda_stream))
+
+        for _ in range(3):
+            produce()
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record(stream)
+        for _ in range(20):
+            produce()
+        p1.record(stream)
+        torch.cuda.synchronize(dev)
+        pms = p0.elapsed_time(p1) / 20
+        pbytes = L_SEQ * HK * D * 2 + NKC * HK * D * 2
+        producer = {"kernel": "compress_keys (k -> k_cmp, not part of the timed step)", "ms": pms,
+                    "gbs": pbytes / (pms * 1e-3) / 1e9, "bytes": pbytes}
+        del k_full
 
     # ---- end to end through the public API with host buffers (pinned), copies timed:
     # this rank's query rows of its kv heads stream in, its top-k ids go back to the host
@@ -490,6 +520,8 @@ def run_ours(args):
             "gpu_launches": (2 + (1 if nrows == L_SEQ else nh)) * args.steps,
             "clocks": clocks,
         }
+        if producer is not None:
+            line["producer"] = producer
         if api is not None:
             am = {k2: statistics.mean(v) for k2, v in api.items()}
             pool_gbs = ab["pool"] / (am["pool"] * 1e-3) / 1e9

@@ -239,6 +239,22 @@ int unum_infllmv2_attn_stage1_noalloc(const void *q, int64_t T, int64_t Hq, int6
                                       int64_t n_seq, float softmax_scale, int causal, void *out,
                                       int64_t out_stride, void *stream);
 
+/*
+ * compress_keys — the producer of stage 1's compressed keys (no reference
+ * function: the reference's caller builds k_cmp; the layout is the one its
+ * stage-1 kernel assumes, the 16-token stride of infllmv2_attn_stage1_triton_v2.py:70).
+ * Compressed key j of sequence b = bf16( sum_{t<kernel} k[cu_seqlens[b] + j*stride + t]
+ * * (1/kernel) ), fp32 sums in token order, round to nearest even.
+ *
+ *   k        bf16 [T, Hk, D=128], strides (k_st, k_sh) elements, 16-byte aligned
+ *   cu_out   int32 [n_seq+1]: cu_out[b+1]-cu_out[b] = (L_b - kernel)/stride + 1, or 0 when
+ *            L_b < kernel; n_out = cu_out[n_seq]
+ *   out      bf16 [n_out, Hk, 128] contiguous
+ */
+int unum_compress_keys(const void *k, int64_t T, int64_t Hk, int64_t D, int64_t k_st, int64_t k_sh,
+                       const int32_t *cu_seqlens, const int32_t *cu_out, int64_t n_seq, int64_t n_out,
+                       int64_t kernel, int64_t stride, void *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -54,6 +54,8 @@ def lib():
         L.oracle_get_block_table.argtypes = [_ptr, _i64, _i64, _i64, _ptr, _i64, _i64, _ptr,
                                              _ptr, ctypes.c_int, _ptr, ctypes.c_int, _i32, _ptr]
         L.oracle_get_block_table.restype = None
+        L.oracle_compress_keys.argtypes = [_ptr, _i64, _ptr, _ptr, _i64, _i64, _i64, _ptr]
+        L.oracle_compress_keys.restype = None
         L.oracle_set_num_threads.argtypes = [ctypes.c_int]
         L.oracle_num_threads.restype = ctypes.c_int
         _lib = L
@@ -158,3 +160,23 @@ def get_block_table(topk_idx, block_table, token_to_bs, token_pos_in_bs, seqlen_
                                      int(pb.size == 1), _p(sq), int(sq.size == 1),
                                      int(head_group), _p(out))
     return out
+
+
+def compressed_counts(seqlens, kernel=32, stride=16):
+    """Compressed keys per sequence: (L - kernel) // stride + 1, 0 when L < kernel."""
+    L = np.asarray(seqlens, np.int64)
+    return np.where(L >= kernel, (L - kernel) // stride + 1, 0)
+
+
+def compress_keys(k, cu_seqlens, kernel=32, stride=16):
+    """Mean-pooled keys (the stage-1 input k_cmp): k [T, Hk, 128] (float values, bf16
+    inputs widened) -> (bf16 bits uint16 [N, Hk, 128], cu_out int32 [B+1])."""
+    k = _c(k, np.float32)
+    cu = _c(cu_seqlens, np.int32)
+    n = compressed_counts(np.diff(cu), kernel, stride)
+    cu_out = np.concatenate([[0], np.cumsum(n)]).astype(np.int32)
+    out = np.zeros((int(cu_out[-1]), k.shape[1], 128), np.uint16)
+    if out.size:
+        lib().oracle_compress_keys(_p(k), k.shape[1], _p(cu), _p(cu_out), len(cu) - 1, int(kernel),
+                                   int(stride), _p(out))
+    return out, cu_out

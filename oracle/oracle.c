@@ -367,3 +367,34 @@ void oracle_get_block_table(const int32_t *topk, int64_t H, int64_t T, int64_t K
                  K,    L,     pos_scalar,  seqlen_scalar,    head_group, out};
     parallel_for(T, 16, gbt_rows, &c);
 }
+
+/* ------------------------------------------------------------------ key compression
+ * The stage-1 input k_cmp from the keys (no reference code: the reference's
+ * caller builds it; the layout follows the 16-token compression stride of
+ * infllmv2_attn_stage1_triton_v2.py:70): compressed key j of sequence b is
+ * bf16(sum_{t<kernel} k[cu_in[b] + j*stride + t] * (1/kernel)), summed in fp32 in
+ * token order, rounded to nearest even; out_bits [cu_out[n_seq], Hk, 128] bf16 bits. */
+static uint16_t f32_to_bf16_rne(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x7FFFFFu)) return (uint16_t)((u >> 16) | 0x40u);
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+void oracle_compress_keys(const float *k, int64_t Hk, const int32_t *cu_in, const int32_t *cu_out,
+                          int64_t n_seq, int64_t kernel, int64_t stride, uint16_t *out_bits) {
+    const float inv = 1.0f / (float)kernel;
+    for (int64_t b = 0; b < n_seq; ++b) {
+        for (int64_t j = 0; j < (int64_t)cu_out[b + 1] - cu_out[b]; ++j) {
+            const int64_t t0 = (int64_t)cu_in[b] + j * stride;
+            for (int64_t h = 0; h < Hk; ++h) {
+                for (int64_t d = 0; d < 128; ++d) {
+                    float acc = 0.f;
+                    for (int64_t t = 0; t < kernel; ++t) acc += k[((t0 + t) * Hk + h) * 128 + d];
+                    out_bits[(((int64_t)cu_out[b] + j) * Hk + h) * 128 + d] = f32_to_bf16_rne(acc * inv);
+                }
+            }
+        }
+    }
+}

@@ -36,6 +36,8 @@ SIGNATURES = {
     "unum_max_pooling_1d_varlen": ([_p, _int, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64,
                                     _i64, _i64, _i64, _p, _p], _int),
     "unum_topk_blocks": ([_p, _int, _i64, _i64, _i64, _i64, _p, _p], _int),
+    "unum_compress_keys": ([_p, _i64, _i64, _i64, _i64, _i64, _p, _p, _i64, _i64, _i64, _i64, _p, _p],
+                           _int),
     "unum_stage1_workspace_size": ([_i64], ctypes.c_size_t),
     "unum_infllmv2_attn_stage1": ([_p, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p,
                                    _p, _i64, ctypes.c_float, _int, _p, _i64, _p, ctypes.c_size_t, _p],
