@@ -159,14 +159,6 @@ __device__ __forceinline__ uint64_t exp2_mufu2(uint64_t x2) {
 
 // Pair p of a strip uses the polynomial when p % mod == mod-1 (mod 0: never);
 // pass 1 and pass 2 have their own share.
-// UNUM_LDPIPE: compute a tile's first 32 columns while its second half loads from TMEM.
-#ifndef UNUM_LDPIPE
-#define UNUM_LDPIPE 0
-#endif
-// UNUM_LD64: read TMEM with one 64-column load instead of two 32-column loads.
-#ifndef UNUM_LD64
-#define UNUM_LD64 0
-#endif
 #ifndef UNUM_POLY_MOD1
 #define UNUM_POLY_MOD1 0
 #endif
@@ -514,30 +506,13 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                     wait_bar(sy, sy.s_full + 8 * buf, (sc >> 1) & 1, 6);
                     tc_fence_after();
                     float v64[64];
-#if UNUM_LDPIPE
-                    // first half, then its compute overlaps the second half's TMEM load
-                    tmem_ld32(tmem + tcol + buf * 256, *reinterpret_cast<float(*)[32]>(&v64[0]));
-                    tmem_wait_ld();
-                    tmem_ld32(tmem + tcol + buf * 256 + 32, *reinterpret_cast<float(*)[32]>(&v64[32]));
-                    p1_chunk<32>(*reinterpret_cast<float(*)[32]>(&v64[0]), kt * kBN + colh, lim_r, c, c2, m, l);
-                    tmem_wait_ld();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(sy.s_empty + 8 * buf);
-                    p1_chunk<32>(*reinterpret_cast<float(*)[32]>(&v64[32]), kt * kBN + colh + 32, lim_r, c, c2, m, l);
-#else
-#if UNUM_LD64
-                    tmem_ld64(tmem + tcol + buf * 256, v64);
-#else
                     tmem_ld32(tmem + tcol + buf * 256, *reinterpret_cast<float(*)[32]>(&v64[0]));
                     tmem_ld32(tmem + tcol + buf * 256 + 32, *reinterpret_cast<float(*)[32]>(&v64[32]));
-#endif
                     tmem_wait_ld();
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(sy.s_empty + 8 * buf);  // values are in registers
                     p1_chunk<64>(v64, kt * kBN + colh, lim_r, c, c2, m, l);
-#endif
                 }
                 part[(wg & 1) * kRows + r] = make_float2(m, l);
                 named_bar_sync(kEpiBarrier, kEpiWarps * 32);
@@ -588,30 +563,14 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                     uint64_t acc[NQ][2];
 #pragma unroll
                     for (int qi = 0; qi < NQ; ++qi) acc[qi][0] = acc[qi][1] = 0ull;
-#if UNUM_LDPIPE
-                    tmem_ld32(tmem + tcol2 + buf * 256, *reinterpret_cast<float(*)[32]>(&w64[0]));
-                    tmem_wait_ld();
-                    tmem_ld32(tmem + tcol2 + buf * 256 + 32, *reinterpret_cast<float(*)[32]>(&w64[32]));
-                    p2_chunk<G, 0>(wa, acc, st4, c2);
-                    tmem_wait_ld();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(sy.s_empty + 8 * buf);
-                    p2_chunk<G, 1>(wb, acc, st4, c2);
-#else
-#if UNUM_LD64
-                    tmem_ld64(tmem + tcol2 + buf * 256, w64);
-#else
                     tmem_ld32(tmem + tcol2 + buf * 256, *reinterpret_cast<float(*)[32]>(&w64[0]));
                     tmem_ld32(tmem + tcol2 + buf * 256 + 32, *reinterpret_cast<float(*)[32]>(&w64[32]));
-#endif
                     tmem_wait_ld();
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(sy.s_empty + 8 * buf);
                     p2_chunk<G, 0>(wa, acc, st4, c2);
                     p2_chunk<G, 1>(wb, acc, st4, c2);
-#endif
                     if (kTmaStore) {
                         // stage the warpgroup's [NQ tokens x 128 keys] tile in shared memory
                         const uint32_t buf_s = stc & 1;
