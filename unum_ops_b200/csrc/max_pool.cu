@@ -65,7 +65,7 @@ __device__ __forceinline__ void store2(T *p, float a, float b, bool paired) {
     }
 }
 
-template <typename T>
+template <typename T, bool kSeg>  // kSeg false: one unit per whole row
 __global__ void __launch_bounds__(kWarps * 32)
 max_pool_kernel(const T *__restrict__ in, int64_t numel, int64_t H, int64_t T_, int64_t fs,
                 const int32_t *__restrict__ cu_q, const int32_t *__restrict__ cu_k,
@@ -81,13 +81,13 @@ max_pool_kernel(const T *__restrict__ in, int64_t numel, int64_t H, int64_t T_, 
     const bool pair_ok = (NB % 2) == 0;  // 2 outputs per lane per vector: aligned word stores
     // work unit = (row, segment of `span` output blocks; span a multiple of 128, so the
     // 16-byte chunks of a segment never straddle its ends): few rows still fill the GPU
-    const int32_t n_seg = (nb + span - 1) / span;
+    const int32_t n_seg = kSeg ? (nb + span - 1) / span : 1;
     const int64_t units = rows * n_seg;
     for (int64_t unit = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); unit < units;
          unit += (int64_t)gridDim.x * kWarps) {
-        const int64_t row = unit / n_seg;
-        const int32_t jA = (int32_t)(unit - row * n_seg) * span;
-        const int32_t jB = jA + span < nb ? jA + span : nb;
+        const int64_t row = kSeg ? unit / n_seg : unit;
+        const int32_t jA = kSeg ? (int32_t)(unit - row * n_seg) * span : 0;
+        const int32_t jB = kSeg ? (jA + span < nb ? jA + span : nb) : nb;
         const int64_t h = row / T_, t = row - h * T_;
         const int b = find_seq(cu_q, n_seq, t);
         int32_t k_len = 0, off_bq = 0;
@@ -230,18 +230,18 @@ extern "C" int unum_max_pooling_1d_varlen(const void *input, int dtype, int64_t 
     const bool vec_ok = unum::aligned16(input) && (fs % vb == 0);
     switch (dtype) {
         case UNUM_DTYPE_F32:
-            max_pool_kernel<float><<<grid, kWarps * 32, 0, s>>>(
+            (n_seg > 1 ? max_pool_kernel<float, true> : max_pool_kernel<float, false>)<<<grid, kWarps * 32, 0, s>>>(
                 (const float *)input, input_numel, H, T, fs, cu_seqlens_q, cu_seqlens_k, cache_lens,
                 n_seq, NB, sp, block_size, init_blocks, local_blocks, vec_ok, span, (float *)out);
             break;
         case UNUM_DTYPE_BF16:
-            max_pool_kernel<__nv_bfloat16><<<grid, kWarps * 32, 0, s>>>(
+            (n_seg > 1 ? max_pool_kernel<__nv_bfloat16, true> : max_pool_kernel<__nv_bfloat16, false>)<<<grid, kWarps * 32, 0, s>>>(
                 (const __nv_bfloat16 *)input, input_numel, H, T, fs, cu_seqlens_q, cu_seqlens_k,
                 cache_lens, n_seq, NB, sp, block_size, init_blocks, local_blocks, vec_ok, span,
                 (__nv_bfloat16 *)out);
             break;
         case UNUM_DTYPE_F16:
-            max_pool_kernel<__half><<<grid, kWarps * 32, 0, s>>>(
+            (n_seg > 1 ? max_pool_kernel<__half, true> : max_pool_kernel<__half, false>)<<<grid, kWarps * 32, 0, s>>>(
                 (const __half *)input, input_numel, H, T, fs, cu_seqlens_q, cu_seqlens_k,
                 cache_lens, n_seq, NB, sp, block_size, init_blocks, local_blocks, vec_ok, span,
                 (__half *)out);
