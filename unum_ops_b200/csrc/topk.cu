@@ -178,13 +178,16 @@ __device__ __forceinline__ void radix_select_with(Fill fill, int32_t K, uint32_t
         __syncwarp();
         fill(pmask, prefix, shift);
         __syncwarp();
-        uint32_t c[8];
+        uint32_t c[8];  // lane owns bins 255-8*lane-i (descending): two 16-byte loads
+        {
+            const uint4 lo4 = reinterpret_cast<const uint4 *>(hist + 248 - 8 * lane)[0];
+            const uint4 hi4 = reinterpret_cast<const uint4 *>(hist + 248 - 8 * lane)[1];
+            c[0] = hi4.w; c[1] = hi4.z; c[2] = hi4.y; c[3] = hi4.x;
+            c[4] = lo4.w; c[5] = lo4.z; c[6] = lo4.y; c[7] = lo4.x;
+        }
         uint32_t s = 0;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {  // lane owns bins 255-8*lane-i (descending)
-            c[i] = hist[255 - 8 * lane - i];
-            s += c[i];
-        }
+        for (int i = 0; i < 8; ++i) s += c[i];
         const uint32_t incl = warp_incl_scan(s, lane);
         const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
         if (p == 0 && total <= (uint32_t)K) {
@@ -253,13 +256,16 @@ __device__ __forceinline__ void select_row16(const uint16_t *rowb, const uint16_
     }
     if (lane == 0 && E > 0) atomicAdd(&hist[hi - t0], (uint32_t)E);
     __syncwarp();
-    uint32_t c[8];
+    uint32_t c[8];  // lane owns bins 255-8*lane-i (descending): two 16-byte loads
+    {
+        const uint4 lo4 = reinterpret_cast<const uint4 *>(hist + 248 - 8 * lane)[0];
+        const uint4 hi4 = reinterpret_cast<const uint4 *>(hist + 248 - 8 * lane)[1];
+        c[0] = hi4.w; c[1] = hi4.z; c[2] = hi4.y; c[3] = hi4.x;
+        c[4] = lo4.w; c[5] = lo4.z; c[6] = lo4.y; c[7] = lo4.x;
+    }
     uint32_t sum = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {  // lane owns bins 255-8*lane-i (descending)
-        c[i] = hist[255 - 8 * lane - i];
-        sum += c[i];
-    }
+    for (int i = 0; i < 8; ++i) sum += c[i];
     const uint32_t incl = warp_incl_scan(sum, lane);
     const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
     __syncwarp();
@@ -401,7 +407,7 @@ __device__ __forceinline__ void emit_bitmap(const uint32_t *selw, const uint32_t
     const int32_t wpl = (nw + 31) >> 5;
     const int32_t w0 = lane * wpl;
     uint32_t sw[kMaxW], tw[kMaxW];
-    uint32_t tc = 0;
+    uint32_t tc = 0, sc = 0;
 #pragma unroll
     for (int i = 0; i < kMaxW; ++i) {
         const bool in = i < wpl && w0 + i < nw;
@@ -409,22 +415,26 @@ __device__ __forceinline__ void emit_bitmap(const uint32_t *selw, const uint32_t
         sw[i] = (in ? selw[w0 + i] : 0u) | (eq_mode == 2 ? ew : 0u);
         tw[i] = eq_mode == 1 ? ew : (in ? tiew[w0 + i] : 0u);
         tc += (uint32_t)__popc(tw[i]);
+        sc += (uint32_t)__popc(sw[i]);
     }
-    const uint32_t tincl = warp_incl_scan(tc, lane);
-    int32_t budget = remaining - (int32_t)(tincl - tc);  // ties left for this lane, in id order
-    uint32_t ns = 0;
+    // one scan for both counts (16 bits each: a row has at most 4096 blocks); ties are taken
+    // in id order, so the lanes before this one take min(remaining, their ties) of them
+    const uint32_t incl = warp_incl_scan((tc << 16) | sc, lane);
+    const int32_t tie_excl = (int32_t)(incl >> 16) - (int32_t)tc;
+    const int32_t sel_excl = (int32_t)(incl & 0xFFFFu) - (int32_t)sc;
+    const int32_t rem = remaining > 0 ? remaining : 0;
+    int32_t budget = rem - tie_excl;  // ties left for this lane, in id order
+    int32_t slot = sel_excl + (tie_excl < rem ? tie_excl : rem);
 #pragma unroll
-    for (int i = 0; i < kMaxW; ++i) {
+    for (int i = 0; i < kMaxW; ++i)
         for (uint32_t m = tw[i]; m != 0u && budget > 0; m &= m - 1u, --budget) sw[i] |= m & (0u - m);
-        ns += (uint32_t)__popc(sw[i]);
-    }
-    const uint32_t sincl = warp_incl_scan(ns, lane);
-    int32_t slot = (int32_t)(sincl - ns);
 #pragma unroll
     for (int i = 0; i < kMaxW; ++i)
         for (uint32_t m = sw[i]; m != 0u && slot < K; m &= m - 1u, ++slot)
             orow[slot] = (w0 + i) * 32 + __ffs(m) - 1;
-    const int32_t total = (int32_t)__shfl_sync(0xffffffffu, sincl, 31);
+    const uint32_t tot = __shfl_sync(0xffffffffu, incl, 31);
+    const int32_t tot_ties = (int32_t)(tot >> 16);
+    const int32_t total = (int32_t)(tot & 0xFFFFu) + (tot_ties < rem ? tot_ties : rem);
     for (int32_t s2 = (total < K ? total : K) + lane; s2 < K; s2 += 32) orow[s2] = -1;
 }
 
