@@ -720,7 +720,7 @@ def run_reference(args):
     line = {
         "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": L_SEQ / v * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "reference",
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f32", "impl": "reference",
         "data": "synthetic (seeded N(0,1) q/k_cmp, random-permutation block table)",
         "config": {"workload": workload_name(),
                    "host": "CPU reference path (C port of the reference semantics, oracle/)"},
