@@ -248,6 +248,7 @@ def run_ours(args):
     from unum_ops_b200.block_select import stage1_pooled
     from unum_ops_b200.infllm_v2 import (_workspace, infllmv2_attn_stage1, max_pooling_1d_varlen,
                                          stage1_status)
+    from unum_ops_b200.sharding import exchange_shards
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -284,16 +285,7 @@ def run_ours(args):
     full_idx = torch.empty(HK, L_SEQ, TOPK, dtype=torch.int32, device=dev)
 
     def gather_idx(local_idx, shards):
-        g, nh_, a, b = shards[rank]
-        full_idx[g:g + nh_, a:b].copy_(local_idx)
-        ops = []
-        for r, (gr, nhr, ar, br) in enumerate(shards):
-            if r == rank:
-                continue
-            ops.append(dist.P2POp(dist.isend, local_idx, r))
-            ops.append(dist.P2POp(dist.irecv, full_idx[gr:gr + nhr, ar:br], r))
-        for w in dist.batch_isend_irecv(ops):
-            w.wait()
+        exchange_shards(local_idx, full_idx, shards, rank)
 
     def step(ev=None):
         """One block-selection pass over this rank's shard: stage 1 with the pooling

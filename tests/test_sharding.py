@@ -102,3 +102,35 @@ def test_prefill_shards_cover_each_head_and_token_once(world):
         work.append((sharding.visible_counts(L, nk)[a:b] + 560.0).sum() * nh)
     assert (cover == 1).all()
     assert max(work) / min(work) < 1.05  # ranges of near-equal work
+
+
+def _exchange_worker(rank, world, port, ret):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    L, K = 4096, 8
+    nk = (L - 32) // 16 + 1
+    ref = torch.arange(2 * L * K, dtype=torch.int32).reshape(2, L, K)
+    shards = [sharding.prefill_shard(world, r, L, nk, 2, token_cost=560.0) for r in range(world)]
+    g, nh, a, b = shards[rank]
+    full = torch.full((2, L, K), -7, dtype=torch.int32)
+    sharding.exchange_shards(ref[g:g + nh, a:b].clone(), full, shards, rank)
+    ret.put((rank, bool(torch.equal(full, ref))))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3, 4])
+def test_exchange_shards_gloo(world):
+    """Every rank ends up with the whole [Hk, T, K] result from the exact-size shards of
+    the others (kv head x query range shards for even rank counts, query ranges else)."""
+    ctx = mp.get_context("spawn")
+    ret = ctx.Queue()
+    port = 30500 + (os.getpid() + world) % 1000
+    procs = [ctx.Process(target=_exchange_worker, args=(r, world, port, ret)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs)
+    got = dict(ret.get(timeout=5) for _ in range(world))
+    assert all(got[r] for r in range(world))

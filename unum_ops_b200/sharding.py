@@ -17,6 +17,7 @@ from __future__ import annotations
 import heapq
 
 import numpy as np
+import torch
 
 
 def visible_counts(q_len: int, k_len: int, causal: bool = True) -> np.ndarray:
@@ -88,3 +89,36 @@ def prefill_shard(world: int, rank: int, q_len: int, k_len: int, n_kv_heads: int
         g, nh, n_r, r = 0, n_kv_heads, world, rank
     a, b = plan_query_ranges(q_len, k_len, n_r, causal, token_cost=token_cost)[r]
     return g, nh, a, b
+
+
+def exchange_shards(local, full, shards, rank, group=None):
+    """Gather every rank's shard of a [Hk, T, ...] result into ``full`` on every rank.
+
+    ``shards[r] = (first kv head, kv heads, t_begin, t_end)`` of rank r (as from
+    ``prefill_shard``); ``local`` is this rank's [kv heads, t_end - t_begin, ...] part.
+    Each rank sends its exact shard to every peer (point-to-point, no padding to the
+    longest shard).  A one-head shard is a contiguous slice of ``full`` and is received
+    in place; a shard of several heads arrives in a contiguous buffer and is copied in.
+    Works with any torch.distributed backend that has send/recv (NCCL on GPUs, gloo on
+    CPU)."""
+    import torch.distributed as dist
+
+    g, nh, a, b = shards[rank]
+    full[g:g + nh, a:b].copy_(local)
+    send = local.contiguous()
+    ops, staged = [], []
+    for r, (gr, nhr, ar, br) in enumerate(shards):
+        if r == rank:
+            continue
+        dst = full[gr:gr + nhr, ar:br]
+        buf = dst if dst.is_contiguous() else torch.empty(dst.shape, dtype=dst.dtype, device=dst.device)
+        if buf is not dst:
+            staged.append((dst, buf))
+        ops.append(dist.P2POp(dist.isend, send, r, group=group))
+        ops.append(dist.P2POp(dist.irecv, buf, r, group=group))
+    if ops:
+        for w in dist.batch_isend_irecv(ops):
+            w.wait()
+    for dst, buf in staged:
+        dst.copy_(buf)
+    return full
