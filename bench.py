@@ -31,6 +31,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -124,7 +125,8 @@ class ClockSampler:
     def __init__(self, index):
         self.index = index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{index}.csv")
+        out_dir = os.environ.get("UNUM_BENCH_CLOCKS_DIR") or tempfile.gettempdir()
+        self.path = os.path.join(out_dir, f"unum_bench_clocks_rank{index}.csv")
 
     def start(self):
         try:

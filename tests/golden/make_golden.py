@@ -3,7 +3,7 @@
 Run in the build container (the reference checkout is not present on GPU
 machines):
 
-    python tests/golden/make_golden.py [--ref /path/to/unum_ops/checkout]
+    python tests/golden/make_golden.py --ref /path/to/unum_ops/checkout   (or UNUM_OPS_REF=...)
 
 It imports the reference's own Python modules straight from its source tree
 (``src/unum_ops/...``) and runs them on CPU:
@@ -77,9 +77,12 @@ def _one_config(kernel):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("UNUM_OPS_REF", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("UNUM_OPS_REF"),
+                    help="checkout of the reference repository (or set UNUM_OPS_REF)")
     ap.add_argument("--only", default="", help="comma list of stage1,pool,gbt")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("pass --ref <reference checkout> or set UNUM_OPS_REF")
     src = os.path.join(args.ref, "src", "unum_ops")
     torch.npu = types.SimpleNamespace(is_available=lambda: False)
     _shim_triton()
