@@ -153,6 +153,14 @@ int unum_topk_blocks(const void *scores, int dtype, int64_t rows, int64_t NB,
  * 16-byte-multiple strides.  workspace: device memory of at least
  * unum_stage1_workspace_size(n_seq) bytes, 16-byte aligned; its contents on
  * entry do not matter.  Calls sharing a workspace must be stream-ordered.
+ *
+ * Two kernels compute this, with the same results: a tile kernel (256/G tokens x
+ * one kv head per work item) and, for batches of at most 4 query tokens per
+ * sequence with G in {16, 32} and out_stride <= 128*512/G, a decode kernel (one
+ * token x one kv head per item, the token's key tiles all held in tensor memory).
+ * A token with more visible keys than out_stride holds sets status 20 in the
+ * decode kernel (see unum_stage1_status); the tile kernel writes the first
+ * out_stride columns.
  */
 size_t unum_stage1_workspace_size(int64_t n_seq);
 
@@ -209,8 +217,10 @@ int unum_infllmv2_attn_stage1_window(const void *q, int64_t T, int64_t Hq, int64
                                      void *stream);
 
 /*
- * Status word a stage-1 launch leaves in its workspace: 0 = ok; nonzero = a
- * bounded wait inside the kernel gave up (the output is then invalid).  Reads
+ * Status word a stage-1 launch leaves in its workspace: 0 = ok; 20 = a token had
+ * more visible keys than out_stride holds (decode kernel; its row is left
+ * unwritten); any other nonzero value = a bounded wait inside the kernel gave up
+ * (the output is then invalid).  Reads
  * the word with a stream-ordered copy and synchronises the stream.
  */
 int unum_stage1_status(const void *workspace, void *stream, int32_t *status_out);
