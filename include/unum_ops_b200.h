@@ -11,7 +11,7 @@
  * uninitialised buffers).
  *
  * Reference interfaces replaced (Yanguan619/unum_ops, Python):
- *   unum_infllmv2_attn_stage1   <- src/unum_ops/infllm_v2/infllmv2_attn_stage1_triton_v2.py:170-245
+ *   unum_infllmv2_attn_stage1   <- src/unum_ops/infllm_v2/infllmv2_attn_stage1_triton_v2.py:153-228
  *                                  (public alias infllm_v2/__init__.py:3-5)
  *   unum_max_pooling_1d_varlen  <- src/unum_ops/infllm_v2/max_pooling_1d_varlen.py:127-183
  *                                  (public alias infllm_v2/__init__.py:7-9)
@@ -133,7 +133,7 @@ int unum_topk_blocks(const void *scores, int dtype, int64_t rows, int64_t NB,
 /*
  * infllmv2_attn_stage1 — compressed-key GQA scores, softmax per head, summed
  * over each head group.  Replaces infllmv2_attn_stage1_triton_v2
- * (infllmv2_attn_stage1_triton_v2.py:170-245; kernel :36-167).
+ * (infllmv2_attn_stage1_triton_v2.py:153-228; kernel :19-150).
  *
  *   q    bf16 [T, Hq, D], strides (q_st, q_sh) elements for t and head, d contiguous
  *   k    bf16 [Tk, Hk, D], strides (k_st, k_sh), d contiguous
@@ -158,9 +158,9 @@ int unum_topk_blocks(const void *scores, int dtype, int64_t rows, int64_t NB,
  * one kv head per work item) and, for batches of at most 4 query tokens per
  * sequence with G in {16, 32} and out_stride <= 128*512/G, a decode kernel (one
  * token x one kv head per item, the token's key tiles all held in tensor memory).
- * A token with more visible keys than out_stride holds sets status 20 in the
- * decode kernel (see unum_stage1_status); the tile kernel writes the first
- * out_stride columns.
+ * A token with more visible keys than out_stride holds (a caller whose
+ * max_seqlen_k is below a sequence's key count) gets the softmax over all its
+ * visible keys with the first out_stride columns written, in both kernels.
  */
 size_t unum_stage1_workspace_size(int64_t n_seq);
 
@@ -217,11 +217,13 @@ int unum_infllmv2_attn_stage1_window(const void *q, int64_t T, int64_t Hq, int64
                                      void *stream);
 
 /*
- * Status word a stage-1 launch leaves in its workspace: 0 = ok; 20 = a token had
- * more visible keys than out_stride holds (decode kernel; its row is left
- * unwritten); any other nonzero value = a bounded wait inside the kernel gave up
- * (the output is then invalid).  Reads
- * the word with a stream-ordered copy and synchronises the stream.
+ * Status word a stage-1 launch leaves in its workspace: 0 = ok; any nonzero
+ * value = a bounded wait inside the kernel gave up (about one second without
+ * progress; the output is then invalid, the kernel drained its in-flight work
+ * and returned, and the context stays usable).  30 = that path taken on purpose:
+ * with the environment variable UNUM_STAGE1_FORCE_EXPIRY=1 at call time every
+ * wait reports expiry at once (a test hook).  Reads the word with a
+ * stream-ordered copy and synchronises the stream.
  */
 int unum_stage1_status(const void *workspace, void *stream, int32_t *status_out);
 
@@ -240,7 +242,9 @@ int unum_stage1_status(const void *workspace, void *stream, int32_t *status_out)
  * (cudaGetSymbolAddress), so make that first call before any stream capture.
  * The call allocates nothing.  All calls on a device share the one array and
  * every call rewrites it fully, so calls that overlap on the GPU (different
- * streams, no ordering between them) race and must be avoided.
+ * streams, no ordering between them) race and must be avoided.  The array's
+ * device address is cached per device for the life of the process: do not use
+ * this entry point across cudaDeviceReset.
  */
 int unum_infllmv2_attn_stage1_noalloc(const void *q, int64_t T, int64_t Hq, int64_t D,
                                       int64_t q_st, int64_t q_sh, const void *k, int64_t Tk,
@@ -248,6 +252,14 @@ int unum_infllmv2_attn_stage1_noalloc(const void *q, int64_t T, int64_t Hq, int6
                                       const int32_t *cu_seqlens_q, const int32_t *cu_seqlens_k,
                                       int64_t n_seq, float softmax_scale, int causal, void *out,
                                       int64_t out_stride, void *stream);
+
+/*
+ * stage1_noalloc_status — the status word (codes as in unum_stage1_status) that
+ * the last unum_infllmv2_attn_stage1_noalloc call on the current device left in
+ * the library's scratch array.  No counterpart in the reference.  Copies the
+ * word on `stream` and synchronises that stream; allocates nothing.
+ */
+int unum_stage1_noalloc_status(void *stream, int32_t *status_out);
 
 /*
  * compress_keys — the producer of stage 1's compressed keys (no reference

@@ -91,7 +91,7 @@ def stage1(q, k, cu_q, cu_k, causal, scale=None, out_stride=None, t_range=None):
 
     q: [T, Hq, D], k: [Tk, Hk, D] (float32 values; bf16 inputs widened).
     out_stride defaults to round-up-128 of the longest compressed sequence,
-    like infllmv2_attn_stage1_triton_v2.py:199-211.  t_range=(a, b) computes
+    like infllmv2_attn_stage1_triton_v2.py:199-225.  t_range=(a, b) computes
     only the rows of tokens a..b-1 and returns [Hk, b-a, out_stride].
     """
     q = _c(q, np.float32)

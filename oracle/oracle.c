@@ -95,7 +95,7 @@ static int find_seq(const int32_t *cu_q, int64_t n_seq, int64_t t) {
 }
 
 /* Number of visible compressed keys for a query.
- * Reference: infllmv2_attn_stage1_triton_v2.py:86-91.  Triton's // on signed
+ * Reference: infllmv2_attn_stage1_triton_v2.py:69-72.  Triton's // on signed
  * integers truncates toward zero (semantic.py lowers it to an sdiv), which is
  * C's / as well: for local_q < 15 the first term is 0, not -1. */
 int64_t oracle_stage1_visible(int64_t local_q, int64_t q_len, int64_t k_len, int causal) {
@@ -108,8 +108,8 @@ int64_t oracle_stage1_visible(int64_t local_q, int64_t q_len, int64_t k_len, int
 
 /* ------------------------------------------------------------------------ */
 /* Stage 1: compressed-key GQA attention scores summed per head group.      */
-/* Reference: infllmv2_attn_stage1_triton_v2.py:36-167 (kernel) and         */
-/* :170-245 (wrapper).                                                      */
+/* Reference: infllmv2_attn_stage1_triton_v2.py:19-150 (kernel) and         */
+/* :153-228 (wrapper).                                                      */
 /*   q   : [T, Hq, D]  values of the bf16 input, widened to float           */
 /*   k   : [Tk, Hk, D] values of the bf16 input, widened to float           */
 /*   out : [Hk, t_end - t_begin, out_stride] float: the rows of tokens      */
@@ -174,7 +174,7 @@ static void stage1_rows(int64_t rb, int64_t re, void *vctx) {
             for (int64_t j = 0; j < wlim; ++j) orow[j] += s[j] * inv;
         }
         for (int64_t j = 0; j < wlim; ++j)
-            if (isnan(orow[j])) orow[j] = 0.f; /* :244 */
+            if (isnan(orow[j])) orow[j] = 0.f; /* :227 */
     }
     free(s);
 }

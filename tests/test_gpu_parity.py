@@ -507,6 +507,68 @@ def test_stage1_decode_kernel_varlen(hq, causal, dev, oracle_lib):
     np.testing.assert_allclose(out.float().cpu().numpy(), orc, atol=ATOL, rtol=RTOL)
 
 
+def test_stage1_decode_rows_longer_than_tensor_memory(dev, oracle_lib, monkeypatch):
+    """A decode batch whose caller passes a max_seqlen_k below a sequence's key count, so
+    a token has more visible keys than the decode kernel's tensor memory holds (G=16:
+    4096): the softmax still runs over every visible key (the keys past the resident
+    tiles on CUDA cores) and the first out_stride columns are written — the same
+    result as the tile kernel and the oracle, and status 0."""
+    from unum_ops_b200.infllm_v2 import infllmv2_attn_stage1, stage1_status
+
+    rng = np.random.default_rng(77)
+    k_lens = np.array([5000, 300, 4096, 9000, 4097, 1], np.int64)
+    q_lens = np.ones(len(k_lens), np.int64)
+    T, Tk = int(q_lens.sum()), int(k_lens.sum())
+    q = rng.standard_normal((T, 32, 128), dtype=np.float32)
+    k = rng.standard_normal((Tk, 2, 128), dtype=np.float32)
+    qb, kb = _t(q, dev, torch.bfloat16), _t(k, dev, torch.bfloat16)
+    cu_q, cu_k = cases.cu(q_lens), cases.cu(k_lens)
+    outs = {}
+    for path in ("decode", "tile"):
+        monkeypatch.setenv("UNUM_STAGE1_PATH", path)
+        outs[path] = infllmv2_attn_stage1(qb, kb, None, _t(cu_q, dev), _t(cu_k, dev), max_seqlen_k=4096,
+                                          causal=True)
+        torch.cuda.synchronize()
+        assert stage1_status(dev) == 0
+    assert outs["decode"].shape[-1] == 4096
+    orc = oracle_lib.stage1(qb.float().cpu().numpy(), kb.float().cpu().numpy(), cu_q, cu_k, True,
+                            out_stride=4096)
+    for path in ("decode", "tile"):
+        np.testing.assert_allclose(outs[path].float().cpu().numpy(), orc, atol=ATOL, rtol=RTOL)
+    np.testing.assert_allclose(outs["decode"].float().cpu().numpy(), outs["tile"].float().cpu().numpy(),
+                               atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("path", ["tile", "decode"])
+def test_stage1_forced_expiry_drains_and_recovers(path, dev, oracle_lib, monkeypatch):
+    """The bounded-wait expiry path, taken on purpose (UNUM_STAGE1_FORCE_EXPIRY=1 makes
+    every wait report expiry before any TMA or UMMA work is issued): the kernel drains,
+    frees tensor memory and returns with status 30; the next normal call on the same
+    workspace returns status 0 and correct scores."""
+    from unum_ops_b200.infllm_v2 import infllmv2_attn_stage1, stage1_status
+
+    rng = np.random.default_rng(5)
+    k_lens = np.array([700, 64, 2000], np.int64)
+    q_lens = np.ones(3, np.int64) if path == "decode" else np.array([300, 17, 1024], np.int64)
+    T, Tk = int(q_lens.sum()), int(k_lens.sum())
+    q = rng.standard_normal((T, 32, 128), dtype=np.float32)
+    k = rng.standard_normal((Tk, 2, 128), dtype=np.float32)
+    qb, kb = _t(q, dev, torch.bfloat16), _t(k, dev, torch.bfloat16)
+    cu_q, cu_k = cases.cu(q_lens), cases.cu(k_lens)
+    monkeypatch.setenv("UNUM_STAGE1_PATH", path)
+    monkeypatch.setenv("UNUM_STAGE1_FORCE_EXPIRY", "1")
+    infllmv2_attn_stage1(qb, kb, None, _t(cu_q, dev), _t(cu_k, dev), causal=path == "tile")
+    torch.cuda.synchronize()
+    assert stage1_status(dev) == 30
+    monkeypatch.delenv("UNUM_STAGE1_FORCE_EXPIRY")
+    out = infllmv2_attn_stage1(qb, kb, None, _t(cu_q, dev), _t(cu_k, dev), causal=path == "tile")
+    torch.cuda.synchronize()
+    assert stage1_status(dev) == 0
+    orc = oracle_lib.stage1(qb.float().cpu().numpy(), kb.float().cpu().numpy(), cu_q, cu_k, path == "tile",
+                            out_stride=out.shape[-1])
+    np.testing.assert_allclose(out.float().cpu().numpy(), orc, atol=ATOL, rtol=RTOL)
+
+
 def test_block_select_graph_replays_new_inputs(dev):
     """BlockSelectGraph: a replay after writing new values into the static inputs gives
     what the eager block_select gives on those values (decode-shaped batch)."""

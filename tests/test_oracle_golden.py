@@ -94,3 +94,31 @@ def test_causal_visible_rule(oracle_lib):
     assert oracle_lib.stage1_visible(0, 1, 777, True) == 777
     # truncating division: chunked prefill q_len=64, k_len=40, local_q=0
     assert oracle_lib.stage1_visible(0, 64, 40, True) == 37
+
+
+@pytest.mark.parametrize("c", cases.gbt_cases(), ids=lambda c: c["name"])
+def test_gbt_torch_restatement_matches_reference(c):
+    """The torch restatement the reference arm of bench.py times (oracle/torch_ref.py)
+    equals the reference's get_block_table_ref_torch outputs."""
+    import torch
+
+    from oracle import torch_ref
+
+    g = _npz("gbt.npz")
+    args = [torch.from_numpy(np.ascontiguousarray(x)) for x in
+            (c["topk"], c["table"], c["token_to_bs"], c["pos"], c["seqlen"])]
+    np.testing.assert_array_equal(torch_ref.get_block_table(*args).numpy(), g[c["name"] + "/out"])
+
+
+def test_topk_torch_restatement_matches_oracle(oracle_lib):
+    """torch.topk + ascending sort (the reference caller's step, as bench.py's reference arm
+    times it) selects the same blocks as the oracle rule on rows without ties."""
+    import torch
+
+    from oracle import torch_ref
+
+    rng = np.random.default_rng(3)
+    p = rng.standard_normal((2, 64, 512)).astype(np.float32)
+    p[:, :, 400:] = -np.inf
+    p[0, :3, 10:] = -np.inf  # rows with fewer candidates than K
+    np.testing.assert_array_equal(torch_ref.topk(torch.from_numpy(p), 64).numpy(), oracle_lib.topk(p, 64))

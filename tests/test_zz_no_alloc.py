@@ -6,7 +6,11 @@ workspace.  This entry point keeps its schedule scratch in a fixed array
 inside the library instead.  The test calls it through the C ABI, twice in a
 row with different batches (so the second call runs on scratch the first one
 left behind), and checks each result against the workspace entry point on the
-same inputs.  It lives in its own file, collected last.
+same inputs, and that the status word it leaves in the library's scratch
+(read with unum_stage1_noalloc_status) is 0.  The batches cover the tile
+kernel, the decode kernel (whose work counter also lives in the scratch) and
+the largest accepted batch, whose schedule fills the scratch array to its
+last word.  It lives in its own file, collected last.
 """
 import ctypes
 
@@ -61,6 +65,56 @@ def test_noalloc_matches_workspace_entry_point_twice():
         torch.cuda.synchronize()
         np.testing.assert_allclose(got.float().cpu().numpy(), ref.float().cpu().numpy(),
                                    atol=ATOL, rtol=RTOL)
+        assert _noalloc_status(L, stream) == 0
+
+
+def _noalloc_status(L, stream):
+    from unum_ops_b200 import _lib
+
+    st = ctypes.c_int32(-1)
+    _lib.check(L.unum_stage1_noalloc_status(stream, ctypes.byref(st)))
+    return st.value
+
+
+def _decode_batch(dev, seed, n_seq, ctx_lo, ctx_hi):
+    """n_seq sequences of one query token each; contexts uniform in [ctx_lo, ctx_hi]."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    ctx = torch.randint(ctx_lo, ctx_hi + 1, (n_seq,), generator=g)
+    k_lens = (ctx - 32) // 16 + 1
+    cu_k = torch.zeros(n_seq + 1, dtype=torch.int32)
+    cu_k[1:] = torch.cumsum(k_lens, 0)
+    q = torch.randn(n_seq, 32, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(int(cu_k[-1]), 2, 128, generator=g).to(torch.bfloat16)
+    cu_q = torch.arange(n_seq + 1, dtype=torch.int32)
+    W = (int(k_lens.max()) + 127) // 128 * 128
+    return q.to(dev), k.to(dev), cu_q.to(dev), cu_k.to(dev), n_seq, W
+
+
+@pytest.mark.gpu
+def test_noalloc_decode_and_largest_batch_back_to_back():
+    """Decode-shaped batches (the decode kernel, whose work counter is scratch word 1)
+    and a batch of exactly the largest accepted sequence count, back to back."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import unum_ops_b200
+    from unum_ops_b200 import _lib
+
+    L = unum_ops_b200.load()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    for seed, n_seq, lo, hi in ((911, 2000, 64, 8192), (912, 1500, 1024, 4096), (913, 16379, 32, 600)):
+        q, k, cu_q, cu_k, n, W = _decode_batch(dev, seed, n_seq, lo, hi)
+        ref = torch.empty(2, q.shape[0], W, dtype=torch.bfloat16, device=dev)
+        ws = torch.empty(L.unum_stage1_workspace_size(n), dtype=torch.uint8, device=dev)
+        _lib.check(L.unum_infllmv2_attn_stage1(*_args(q, k, cu_q, cu_k, n, ref, W),
+                                               ws.data_ptr(), ws.numel(), stream))
+        got = torch.full_like(ref, float("nan"))
+        _lib.check(L.unum_infllmv2_attn_stage1_noalloc(*_args(q, k, cu_q, cu_k, n, got, W), stream))
+        torch.cuda.synchronize()
+        np.testing.assert_allclose(got.float().cpu().numpy(), ref.float().cpu().numpy(),
+                                   atol=ATOL, rtol=RTOL)
+        assert _noalloc_status(L, stream) == 0
 
 
 @pytest.mark.gpu

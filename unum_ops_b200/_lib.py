@@ -43,6 +43,7 @@ SIGNATURES = {
                                    _p, _i64, ctypes.c_float, _int, _p, _i64, _p, ctypes.c_size_t, _p],
                                   _int),
     "unum_stage1_status": ([_p, _p, ctypes.POINTER(_i32)], _int),
+    "unum_stage1_noalloc_status": ([_p, ctypes.POINTER(_i32)], _int),
     "unum_infllmv2_attn_stage1_pooled": ([_p, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64,
                                           _i64, _p, _p, _i64, ctypes.c_float, _int, _p, _i64, _p,
                                           _i64, _i64, _i64, _p, ctypes.c_size_t, _p], _int),

@@ -1,11 +1,11 @@
 // infllmv2_attn_stage1 on B200: tcgen05 (TMEM) tensor-core kernel.
 //
 // Semantics follow the public Triton kernel of the reference
-// (src/unum_ops/infllm_v2/infllmv2_attn_stage1_triton_v2.py:36-167, wrapper
-// :170-245): for kv head g and token t,
+// (src/unum_ops/infllm_v2/infllmv2_attn_stage1_triton_v2.py:19-150, wrapper
+// :153-228): for kv head g and token t,
 //     out[g,t,j] = sum_{h in group g} softmax_j(q[t,h] . k[k_start+j,g] * scale)
-// over the keys visible to t (causal rule :86-91), 0 elsewhere and 0 for an
-// empty softmax (the reference's NaN -> 0, :244).
+// over the keys visible to t (causal rule :69-72), 0 elsewhere and 0 for an
+// empty softmax (the reference's NaN -> 0, :227).
 //
 // Work decomposition.  A tile is QT = 256/G consecutive tokens of one sequence
 // and one kv head: its 256 (token, head) rows of Q (64 KB bf16, loaded once by
@@ -92,6 +92,10 @@ constexpr int kWsTiles = 4;
 
 struct Params {
     const int32_t *cu_q;
+    // compressed keys as plain memory (strides in elements), for the decode kernel's
+    // keys beyond tensor-memory capacity
+    const __nv_bfloat16 *k;
+    int64_t k_st, k_sh;
     const int32_t *cu_k;
     int32_t *ws;
     __nv_bfloat16 *out;
@@ -107,6 +111,9 @@ struct Params {
     int32_t NB, init_blocks, local_blocks;
     // token window: only tiles whose tokens intersect [t_begin, t_end) are computed
     int64_t t_begin, t_end;
+    // nonzero: every bounded wait reports expiry at once (status 30) before any
+    // TMA or UMMA work is issued, so the drain path can be tested without a fault
+    int32_t force_expiry;
 };
 
 struct Item {
@@ -129,26 +136,29 @@ __device__ __forceinline__ int32_t visible(int32_t lq, int32_t q_len, int32_t k_
 // 2^x on the FMA pipe for two values at once, for a share of the
 // exponentials so the MUFU (ex2) pipe — 16 results per clock per SM — is not
 // the only unit doing them.  Split x = j + f with j = round(x) (adding
-// 1.5*2^23 rounds to an integer in the low mantissa bits) and f in
-// [-0.5, 0.5]; 2^f by a cubic fitted here to minimise the maximum relative
-// error on that interval (7.5e-5, far below the bf16 output precision); 2^j by
-// adding j to the exponent field.  Inputs are clamped to >= -126, so a masked
-// (-inf) score yields 2^-126 instead of 0 — negligible in any sum here; masked
-// outputs are written as exact zeros separately.
+// 1.5*2^23 rounds to an integer held in the low mantissa bits) and f in
+// [-0.5, 0.5]; 2^f by a cubic fitted to minimise the maximum relative error on
+// that interval (7.5e-5, far below the bf16 output precision); 2^j by adding
+// j to the exponent field (one integer multiply-add per value).  Inputs are
+// clamped to >= -126, so a score far below the row maximum yields about 2^-126
+// instead of a smaller number — negligible in any sum here.
 __device__ __forceinline__ uint64_t exp2_fma2(uint64_t x2) {
     float lo, hi;
     f2_unpack(x2, lo, hi);
     x2 = f2_pack(fmaxf(lo, -126.0f), fmaxf(hi, -126.0f));
     const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);
     const uint64_t nmagic = f2_pack(-12582912.0f, -12582912.0f);
-    const uint64_t t = f2_add(x2, magic);
-    const uint64_t f = f2_fma(f2_add(t, nmagic), f2_pack(-1.0f, -1.0f), x2);  // x - round(x)
+    const uint64_t t = f2_add(x2, magic);                                   // 1.5*2^23 + j
+    const uint64_t f = f2_fma(f2_add(t, nmagic), f2_pack(-1.0f, -1.0f), x2);  // x - j
     uint64_t p = f2_fma(f2_pack(0.055171460f, 0.055171460f), f, f2_pack(0.24261086f, 0.24261086f));
     p = f2_fma(p, f, f2_pack(0.69326097f, 0.69326097f));
     p = f2_fma(p, f, f2_pack(0.99992812f, 0.99992812f));
-    const uint32_t plo = (uint32_t)p, phi = (uint32_t)(p >> 32);
-    const uint32_t tlo = (uint32_t)t, thi = (uint32_t)(t >> 32);
-    return (uint64_t)(plo + (tlo << 23)) | ((uint64_t)(phi + (thi << 23)) << 32);
+    // bits(2^f) + (j << 23): the low 9 bits of bits(t) hold j (two's complement) and
+    // the magic's own bits shift out of the word
+    uint32_t rlo, rhi;
+    asm("mad.lo.u32 %0, %1, 8388608, %2;" : "=r"(rlo) : "r"((uint32_t)t), "r"((uint32_t)p));
+    asm("mad.lo.u32 %0, %1, 8388608, %2;" : "=r"(rhi) : "r"((uint32_t)(t >> 32)), "r"((uint32_t)(p >> 32)));
+    return (uint64_t)rlo | ((uint64_t)rhi << 32);
 }
 
 __device__ __forceinline__ uint64_t exp2_mufu2(uint64_t x2) {
@@ -203,14 +213,21 @@ struct Sync {
     int32_t *status;
 };
 
+#ifndef UNUM_WAIT_HINT_NS
+#define UNUM_WAIT_HINT_NS 0
+#endif
 // Bounded wait: false once this CTA has given up (then callers stop issuing work).
 __device__ __forceinline__ bool wait_bar(const Sync &s, uint32_t bar, uint32_t parity, int code) {
     if (*s.abort) return false;
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t_start = globaltimer_ns();
     for (uint32_t i = 1;; ++i) {
+#if UNUM_WAIT_HINT_NS > 0
+        if (mbar_try_wait_sleep(bar, parity, UNUM_WAIT_HINT_NS)) return true;
+#else
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 63) == 0) {
+#endif
+        if ((i & (UNUM_WAIT_HINT_NS > 0 ? 3u : 63u)) == 0) {
             if (*s.abort) return false;
             if (globaltimer_ns() - t_start > kWaitNs) {
                 *s.abort = 1;
@@ -238,7 +255,14 @@ __device__ __forceinline__ void p1_chunk(float (&v)[N], int32_t colbase, int32_t
     if (mt == -INFINITY) return;
     const uint64_t nmc = f2_pack(-mt * c, -mt * c);
     uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+#ifndef UNUM_P1_SCALAR
+#define UNUM_P1_SCALAR 0
+#endif
+#if UNUM_P1_SCALAR
+#define UNUM_P1(P) if ((P) < N / 2) { float lo_, hi_, e0_, e1_; f2_unpack(exp2_pair_mod<UNUM_POLY_MOD1, P>(f2_fma(f2_pack(v[2 * (P)], v[2 * (P) + 1]), c2, nmc)), e0_, e1_); f2_unpack(acc[(P) & 3], lo_, hi_); acc[(P) & 3] = f2_pack(lo_ + e0_, hi_ + e1_); }
+#else
 #define UNUM_P1(P) if ((P) < N / 2) acc[(P) & 3] = f2_add(acc[(P) & 3], exp2_pair_mod<UNUM_POLY_MOD1, P>(f2_fma(f2_pack(v[2 * (P)], v[2 * (P) + 1]), c2, nmc)));
+#endif
 #define UNUM_P1x4(P) UNUM_P1(P) UNUM_P1(P + 1) UNUM_P1(P + 2) UNUM_P1(P + 3)
     UNUM_P1x4(0) UNUM_P1x4(4) UNUM_P1x4(8) UNUM_P1x4(12)
     UNUM_P1x4(16) UNUM_P1x4(20) UNUM_P1x4(24) UNUM_P1x4(28)
@@ -252,6 +276,14 @@ __device__ __forceinline__ void p1_chunk(float (&v)[N], int32_t colbase, int32_t
     m = mt;
 }
 
+#ifndef UNUM_P2_SCALAR
+#define UNUM_P2_SCALAR 0
+#endif
+#if UNUM_P2_SCALAR
+#define UNUM_P2ACC(A, E) { float lo_, hi_, e0_, e1_; f2_unpack((E), e0_, e1_); f2_unpack((A), lo_, hi_); (A) = f2_pack(lo_ + e0_, hi_ + e1_); }
+#else
+#define UNUM_P2ACC(A, E) (A) = f2_add((A), (E));
+#endif
 // Pass 2 on accumulator columns H*32..H*32+31 of this warpgroup (key = TMEM lane):
 // add exp2(s*c - b) into the per-token head sums.
 template <int G, int H>
@@ -260,7 +292,8 @@ __device__ __forceinline__ void p2_chunk(const float (&v)[32], uint64_t (&acc)[6
 #define UNUM_P2(P, SV)                                                                              \
     {                                                                                               \
         const uint64_t x2 = f2_fma(f2_pack(v[2 * (P)], v[2 * (P) + 1]), c2, SV);                    \
-        acc[(H * 32 + 2 * (P)) / G][(P) & 1] = f2_add(acc[(H * 32 + 2 * (P)) / G][(P) & 1], exp2_pair_mod<UNUM_POLY_MOD2, H * 16 + (P)>(x2)); \
+        const uint64_t e2 = exp2_pair_mod<UNUM_POLY_MOD2, H * 16 + (P)>(x2);                         \
+        UNUM_P2ACC(acc[(H * 32 + 2 * (P)) / G][(P) & 1], e2);                                         \
     }
 #define UNUM_P2x2(P)                                                                                \
     {                                                                                               \
@@ -367,6 +400,10 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
             mbar_init(sy.s_empty + 8 * b, kEpiWarps);
         }
         *abort_flag = 0;
+        if (p.force_expiry) {
+            *abort_flag = 1;
+            atomicCAS(p.ws, 0, 30);
+        }
         fence_barrier_init();
     }
     if (warp == kProducerWarp && lane == 0) {
@@ -512,7 +549,11 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(sy.s_empty + 8 * buf);  // values are in registers
+#ifndef UNUM_ABL_P1
                     p1_chunk<64>(v64, kt * kBN + colh, lim_r, c, c2, m, l);
+#else
+                    m = fmaxf(m, v64[kt & 63]);
+#endif
                 }
                 part[(wg & 1) * kRows + r] = make_float2(m, l);
                 named_bar_sync(kEpiBarrier, kEpiWarps * 32);
@@ -569,8 +610,12 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(sy.s_empty + 8 * buf);
+#ifndef UNUM_ABL_P2
                     p2_chunk<G, 0>(wa, acc, st4, c2);
                     p2_chunk<G, 1>(wb, acc, st4, c2);
+#else
+                    acc[0][0] = __float_as_uint(wa[kt & 31]);
+#endif
                     if (kTmaStore) {
                         // stage the warpgroup's [NQ tokens x 128 keys] tile in shared memory
                         const uint32_t buf_s = stc & 1;
@@ -879,9 +924,11 @@ struct DecItem {
     bool active;      // false: token outside every sequence or outside the token window
 };
 
-// An item needing more than max_tiles key tiles (more visible keys than the
-// out_stride the caller sized the output for allows) gets nkt = 0, vis = -1:
-// nothing is computed and the epilogue reports it in the status word.
+// An item with more than max_tiles key tiles (more visible keys than tensor
+// memory holds; only when the caller's out_stride is below a sequence's key
+// count) keeps its full visible count in vis but only max_tiles tiles in nkt:
+// the epilogue folds the keys past them into the softmax statistics on CUDA
+// cores (dec_extra_scores).  Their columns lie past out_stride, so none is written.
 __device__ __forceinline__ DecItem dec_decode(int64_t w, const Params &p, int32_t max_tiles) {
     DecItem it;
     it.g = (int32_t)(w % p.Hk);
@@ -904,10 +951,7 @@ __device__ __forceinline__ DecItem dec_decode(int64_t w, const Params &p, int32_
     const int32_t k_len = __ldg(p.cu_k + lo + 1) - (int32_t)it.k_start;
     it.vis = visible(t - qs, q_len, k_len, p.causal);
     it.nkt = (it.vis + kBN - 1) / kBN;
-    if (it.nkt > max_tiles) {
-        it.nkt = 0;
-        it.vis = -1;
-    }
+    if (it.nkt > max_tiles) it.nkt = max_tiles;
     it.active = true;
     return it;
 }
@@ -947,6 +991,39 @@ __device__ __forceinline__ bool named_bar_or(int id, int n, bool pred) {
         "bar.red.or.pred p, %2, %3, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(r) : "r"((uint32_t)pred), "r"(id), "r"(n) : "memory");
     return r != 0;
+}
+
+// Raw scores q[t, h] . k[k_start + j, g] of heads h0..h0+7 of a decode item for
+// one key j past the item's tensor-memory tiles, on CUDA cores: q from the
+// item's shared-memory tile (two 64-column panels, 128-byte swizzle: 16-byte
+// chunk c of row h sits at chunk c ^ (h & 7)), k from global memory.  Products
+// of bf16 values are exact in f32, so these match the tensor-core scores up to
+// the order of the sums.
+template <int G>
+__device__ __forceinline__ void dec_extra_scores8(const Params &p, const uint8_t *qtile, int32_t g,
+                                                  int64_t k_start, int32_t j, int h0, float (&sc)[8]) {
+    const uint4 *kr = reinterpret_cast<const uint4 *>(p.k + (k_start + j) * p.k_st + (int64_t)g * p.k_sh);
+#pragma unroll
+    for (int h = 0; h < 8; ++h) sc[h] = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 16; ++c) {
+        const uint4 kv = __ldg(kr + c);
+        const __nv_bfloat162 *k2 = reinterpret_cast<const __nv_bfloat162 *>(&kv);
+        const uint8_t *panel = qtile + (c >> 3) * (G * 128);
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+            const int hh = h0 + h;
+            const uint4 qv = *reinterpret_cast<const uint4 *>(panel + hh * 128 + (((c & 7) ^ (hh & 7)) << 4));
+            const __nv_bfloat162 *q2 = reinterpret_cast<const __nv_bfloat162 *>(&qv);
+            float a = sc[h];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                a = fmaf(__low2float(q2[e]), __low2float(k2[e]), a);
+                a = fmaf(__high2float(q2[e]), __high2float(k2[e]), a);
+            }
+            sc[h] = a;
+        }
+    }
 }
 
 template <int G>
@@ -989,6 +1066,10 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
         for (int i = 0; i < kDecSlots; ++i) mbar_init(tmem_full + 8 * i, 1);
         for (uint32_t i = 0; i < kTs; ++i) mbar_init(slot_empty + 8 * i, 4);  // a tile's 4 reader warps
         *abort_flag = 0;
+        if (p.force_expiry) {
+            *abort_flag = 1;
+            atomicCAS(p.ws, 0, 30);
+        }
         fence_barrier_init();
     }
     if (warp == kDecProducerWarp && lane == 0) {
@@ -1093,7 +1174,6 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
             const int64_t w = item_id[s];
             if (w < 0) break;
             const DecItem it = dec_decode(w, p, (int32_t)kTmemCols / G);
-            if (it.vis < 0 && tid == 0) atomicCAS(p.ws, 0, 20);  // more keys than out_stride holds
             __nv_bfloat16 *orow = p.out + ((int64_t)it.g * p.T + it.t) * p.out_stride;
             int32_t zero_from = 0;  // first column of the row to zero-fill
             if (it.active && it.nkt > 0) {
@@ -1122,6 +1202,18 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                         }
                     }
                 }
+                // keys past the tensor-memory tiles (an out_stride below the sequence's key
+                // count): into the statistics only, on CUDA cores
+                const uint8_t *qtile = sgen + s * kDecQSlot;
+                for (int32_t j = it.nkt * kBN + tid; j < it.vis; j += kDecEpiWarps * 32) {
+#pragma unroll
+                    for (int h0 = 0; h0 < G; h0 += 8) {
+                        float sc[8];
+                        dec_extra_scores8<G>(p, qtile, it.g, it.k_start, j, h0, sc);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) m[h0 + i] = fmaxf(m[h0 + i], sc[i]);
+                    }
+                }
                 dec_reduce<G, true>(m, red, warp, lane);
 #pragma unroll
                 for (int i = 0; i < G; ++i) l[i] = 0.f;
@@ -1133,6 +1225,15 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
 #pragma unroll
                             for (int i = 0; i < G; ++i) l[i] += ex2((vb[b][i] - m[i]) * c);
                         }
+                    }
+                }
+                for (int32_t j = it.nkt * kBN + tid; j < it.vis; j += kDecEpiWarps * 32) {
+#pragma unroll
+                    for (int h0 = 0; h0 < G; h0 += 8) {
+                        float sc[8];
+                        dec_extra_scores8<G>(p, qtile, it.g, it.k_start, j, h0, sc);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) l[h0 + i] += ex2((sc[i] - m[h0 + i]) * c);
                     }
                 }
                 dec_reduce<G, false>(l, red + kDecEpiWarps * 32, warp, lane);
@@ -1164,7 +1265,7 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                 named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);  // every thread has read item_id[s]
             }
             if (tid == 0) mbar_arrive(item_empty + 8 * s);
-            if (it.active && it.vis >= 0 && zero_from < p.out_stride) {
+            if (it.active && zero_from < p.out_stride) {
                 const int32_t n16 = (int32_t)((p.out_stride - zero_from) >> 3);
                 uint4 *dst = reinterpret_cast<uint4 *>(orow + zero_from);
                 for (int32_t e = tid; e < n16; e += kDecEpiWarps * 32) dst[e] = make_uint4(0u, 0u, 0u, 0u);
@@ -1251,6 +1352,10 @@ int stage1_run(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, in
     cudaStream_t s = (cudaStream_t)stream;
     int32_t *ws = (int32_t *)workspace;
     const int QT = (int)(kRows / G);
+    // test hook: UNUM_STAGE1_FORCE_EXPIRY=1 makes the main kernel take its expiry
+    // path (status 30, output invalid) without waiting, to exercise the drain
+    const char *fe = getenv("UNUM_STAGE1_FORCE_EXPIRY");
+    const int32_t force_expiry = (fe && fe[0] == '1') ? 1 : 0;
     stage1_prologue<<<1, 1024, 0, s>>>(cu_seqlens_q, (int32_t)n_seq, QT, ws,
                                        (__nv_bfloat16 *)out, T, (int32_t)Hk, out_stride,
                                        (__nv_bfloat16 *)pooled, (int32_t)NB, (int32_t)init_blocks,
@@ -1298,6 +1403,10 @@ int stage1_run(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, in
         p.local_blocks = 0;
         p.t_begin = t_begin;
         p.t_end = t_end;
+        p.k = (const __nv_bfloat16 *)k;
+        p.k_st = k_st;
+        p.k_sh = k_sh;
+        p.force_expiry = force_expiry;
         return G == 16 ? launch_decode<16>(mqd, mk, p, s) : launch_decode<32>(mqd, mk, p, s);
     }
     CUtensorMap mo;  // out as a 2-D [Hk*T, out_stride] bf16 tensor, [64/G x 128] store boxes
@@ -1332,6 +1441,10 @@ int stage1_run(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, in
     p.local_blocks = (int32_t)local_blocks;
     p.t_begin = t_begin;
     p.t_end = t_end;
+    p.k = (const __nv_bfloat16 *)k;
+    p.k_st = k_st;
+    p.k_sh = k_sh;
+    p.force_expiry = force_expiry;
     switch (G) {
         case 2: return launch_main<2>(mq, mk, mo, p, T, s);
         case 4: return launch_main<4>(mq, mk, mo, p, T, s);
@@ -1428,7 +1541,10 @@ std::mutex g_scratch_mu;
 void *g_scratch_ptr[kMaxDevices] = {nullptr};
 
 // Device address of g_stage1_scratch on the current device (looked up once per
-// device; host code cannot use the symbol itself as a device pointer).
+// device; host code cannot use the symbol itself as a device pointer).  The
+// address is cached for the life of the process: after cudaDeviceReset (or
+// any other teardown of the device's primary context) the module may load at
+// another address, so these entry points must not be used across a reset.
 int scratch_for_current_device(void **out) {
     int dev = 0;
     UNUM_CHECK_CUDA(cudaGetDevice(&dev));
@@ -1469,4 +1585,16 @@ extern "C" int unum_infllmv2_attn_stage1_noalloc(const void *q, int64_t T, int64
     return unum_infllmv2_attn_stage1(q, T, Hq, D, q_st, q_sh, k, Tk, Hk, k_st, k_sh, cu_seqlens_q,
                                      cu_seqlens_k, n_seq, softmax_scale, causal, out, out_stride,
                                      scratch, kNoAllocBytes, stream);
+}
+
+// Status word of the last unum_infllmv2_attn_stage1_noalloc call on the current
+// device (word 0 of the library's scratch array): the same codes as
+// unum_stage1_status.  Reads it with a stream-ordered copy and synchronises the
+// stream, so pass the stream the stage-1 call was made on.
+extern "C" int unum_stage1_noalloc_status(void *stream, int32_t *status_out) {
+    unum::clear_error();
+    UNUM_CHECK_ARG(status_out != nullptr, "null pointer argument");
+    void *scratch = nullptr;
+    if (int rc = scratch_for_current_device(&scratch)) return rc;
+    return unum_stage1_status(scratch, stream, status_out);
 }

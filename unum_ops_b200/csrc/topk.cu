@@ -30,16 +30,9 @@ namespace {
 constexpr int kWarps = 4;
 constexpr int kMaxNB = 4096;
 constexpr int kMaxK = 1024;
-#ifndef UNUM_TOPK_CAND
-#define UNUM_TOPK_CAND 640
-#endif
-constexpr int kCandCap = UNUM_TOPK_CAND;  // candidate buffer per warp (a multiple of 32)
-#ifndef UNUM_TOPK_SHRINK
-#define UNUM_TOPK_SHRINK 4  // 16-bit path: narrow the margin once more than 1/4 of the slots fill
-#endif
-#ifndef UNUM_TOPK_MINBLOCKS
-#define UNUM_TOPK_MINBLOCKS 7
-#endif
+constexpr int kCandCap = 640;  // candidate buffer per warp (a multiple of 32)
+constexpr int kShrink = 4;     // 16-bit path: narrow the margin once more than 1/kShrink of the slots fill
+constexpr int kMinBlocks16 = 7;  // resident blocks per SM asked of the 16-bit instance
 
 template <typename T> __device__ __forceinline__ float to_f(T v);
 template <> __device__ __forceinline__ float to_f<float>(float v) { return v; }
@@ -480,7 +473,7 @@ template <> __device__ __forceinline__ float key_value<float>(uint32_t k) {
 // more than the slots hold) the row is staged in shared memory as keys and the
 // full radix select runs on it.  Results never depend on which path ran.
 template <typename T, int kMaxW>  // kMaxW: 2 for rows of at most 2048 blocks, else 4
-__global__ void __launch_bounds__(kWarps * 32, sizeof(T) == 2 ? UNUM_TOPK_MINBLOCKS : 1)  // 16-bit: 7 blocks, <= 72 registers
+__global__ void __launch_bounds__(kWarps * 32, sizeof(T) == 2 ? kMinBlocks16 : 1)  // 16-bit: 7 blocks, <= 72 registers
 topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_stride, int32_t K,
             bool vec_ok, int64_t rows_per_warp, int32_t *__restrict__ out) {
     using Key = typename KeyOf<T>::K;
@@ -572,7 +565,7 @@ topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_
                 const bool ovf = __any_sync(0xffffffffu, cnt > (uint32_t)kLaneCand);
                 const bool under = n_st + E < K;  // the threshold lies below t0
                 if (ovf) margin = margin / 2 > kMarginMin ? margin / 2 : kMarginMin;
-                else if (n_st > kCandCap / UNUM_TOPK_SHRINK) margin = margin - margin / 4 > kMarginMin ? margin - margin / 4 : kMarginMin;
+                else if (n_st > kCandCap / kShrink) margin = margin - margin / 4 > kMarginMin ? margin - margin / 4 : kMarginMin;
                 else if (under && t0 > kMinFinite<T>) margin = margin * 2 < kMarginMax ? margin * 2 : kMarginMax;
                 __syncwarp();
                 if (!ovf && !under) {

@@ -65,11 +65,16 @@ def infllmv2_attn_stage1(
 ):
     """Stage-1 compressed attention scores summed per kv-head group.
 
-    Mirrors infllmv2_attn_stage1_triton_v2 (infllmv2_attn_stage1_triton_v2.py:170-245):
+    Mirrors infllmv2_attn_stage1_triton_v2 (infllmv2_attn_stage1_triton_v2.py:153-228):
     q [total_q, n_heads, head_dim], k [total_k, n_kv_heads, head_dim] (cast to bf16
     like the reference kernel's loads), int32 cu_seqlens; returns bf16
     [n_kv_heads, total_q, round_up(max_seqlen_k, 128)].  ``v`` and the
     flash-attn-style extra arguments are accepted and ignored, as in the reference.
+
+    The call is asynchronous.  Every row is written by the kernels; the one failure
+    they can report is a bounded wait inside the kernel that gave up (about a second
+    without progress), which leaves the output invalid: callers that must detect it
+    read ``stage1_status()`` (nonzero) after the call, which synchronises the stream.
     """
     dev = _lib.require_cuda(q, k, cu_seqlens_q, cu_seqlens_k)
     q, k = [x.contiguous() if x.stride(-1) != 1 else x for x in (q, k)]
