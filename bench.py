@@ -287,9 +287,11 @@ def run_ours(args):
     # each rank's full [Hk, T, K] buffer (NCCL point-to-point, no padding)
     ranges = [shard_of(world, r, strong) for r in range(world)]
     full_idx = torch.empty(HK, L_SEQ, TOPK, dtype=torch.int32, device=dev)
+    # the ids travel as int16 (block ids < NB <= 2^15, -1 padding kept): half the bytes
+    wire_idx = torch.empty(HK, L_SEQ, TOPK, dtype=torch.int16, device=dev)
 
     def gather_idx(local_idx, shards):
-        exchange_shards(local_idx, full_idx, shards, rank)
+        exchange_shards(local_idx, full_idx, shards, rank, wire=wire_idx)
 
     def step(ev=None):
         """One block-selection pass over this rank's shard: stage 1 with the pooling
@@ -408,6 +410,16 @@ def run_ours(args):
                     "gbs": pbytes / (pms * 1e-3) / 1e9, "bytes": pbytes}
         del k_full
 
+    # ---- the config-4 decode batch (and the stage-2 consumer on it) at the same N, as
+    # context in the same line
+    decode = None
+    if args.decode_batch > 0:
+        torch.cuda.empty_cache()
+        decode = measure_decode(args, world, rank, dev, steps=max(args.steps, 20), warmup=max(args.warmup, 3))
+        torch.cuda.empty_cache()
+        decode["stage2"] = measure_stage2(args, world, rank, dev)
+        torch.cuda.empty_cache()
+
     # ---- end to end through the public API with host buffers (pinned), copies timed:
     # this rank's query rows of its kv heads stream in, its top-k ids go back to the host
     # (end to end the shards balance the host-to-device copy: near-equal token ranges)
@@ -459,7 +471,7 @@ def run_ours(args):
         traffic = load_traffic()
         s1_tf = flops / (mean["stage1"] * 1e-3) / 1e12
         kernels = {
-            "stage1": {"ms": mean["stage1"], "tflops": s1_tf, "frac": s1_tf / tf_sus,
+            "stage1": {"ms": mean["stage1"], "tflops": s1_tf, "frac": s1_tf / tf_burst,
                        "bound": "tensor", "fused": "max_pooling_1d_varlen",
                        "out_gbs": ab["stage1_out"] / (mean["stage1"] * 1e-3) / 1e9},
         }
@@ -467,8 +479,9 @@ def run_ours(args):
             gbs = ab[kname] / (mean[kname] * 1e-3) / 1e9
             kernels[kname] = {"ms": mean[kname], "gbs": gbs, "frac": gbs / hbm, "bound": "hbm"}
         if world > 1:
-            kernels["topk_idx_gather"] = {"ms": mean["gather"], "bytes": full_idx.numel() * 4,
-                                          "how": "NCCL send/recv of each rank's exact shard"}
+            kernels["topk_idx_gather"] = {"ms": mean["gather"], "bytes": full_idx.numel() * 2,
+                                          "how": "NCCL send/recv of each rank's exact shard, int16 "
+                                                 "on the wire, widened to int32 once"}
         cpu = None
         if args.cpu_sample > 0 and world == 1:
             hf = {k: v.numpy() for k, v in host.items() if k not in ("q", "k")}
@@ -499,11 +512,14 @@ def run_ours(args):
                        "rank0_shard": {"kv_heads": [g0, g0 + nh], "tokens": [ta, tb_]},
                        "l2": "inputs larger than L2 (q 1.07 GB, scores 4.3 GB, slots 4.3 GB)"},
             "roofline": {"bound": "tensor", "kernel": "stage1", "achieved": s1_tf,
-                         "peak": tf_sus, "unit": "TFLOP/s", "frac": s1_tf / tf_sus,
-                         "peak_source": f"{src} bf16_tflops_sustained",
+                         "peak": tf_burst, "unit": "TFLOP/s", "frac": s1_tf / tf_burst,
+                         "peak_source": f"{src} bf16_tflops (burst: the timed region is a fraction of a second)",
+                         "frac_of_sustained": s1_tf / tf_sus,
                          "algorithmic": "2*D*G*sum_t visible(t) over rank 0's shard = %.4g flop "
                                         "per launch" % flops,
                          "traffic": traffic.get("stage1") if world == 1 else None,
+                         "traffic_source": "profiles/traffic_c3.json (ncu dram bytes at 32k and 64k, "
+                                           "derived per term for 128k)" if world == 1 else None,
                          "mufu": mufu_roofline(flops, mean["stage1"], clocks)},
             "kernels": kernels,
             "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
@@ -518,6 +534,8 @@ def run_ours(args):
         }
         if producer is not None:
             line["producer"] = producer
+        if decode is not None:
+            line["decode"] = decode
         if api is not None:
             am = {k2: statistics.mean(v) for k2, v in api.items()}
             pool_gbs = ab["pool"] / (am["pool"] * 1e-3) / 1e9
@@ -534,26 +552,20 @@ def run_ours(args):
 
 
 # ------------------------------------------------------------------ decode batch (config 4)
-def run_decode(args):
+def measure_decode(args, world, rank, dev, steps=None, warmup=None):
     """512 sequences x 1 query token, contexts U[4096, 65536].  A step is
-    block_select on the batch.  With N ranks the batch is split by longest-processing-time
-    packing of the sequences' compressed-key counts (strong scaling; --scaling weak gives
-    every rank its own batch) and the top-k ids are all-gathered inside the step."""
+    block_select on the batch (one CUDA-graph replay).  With N ranks the batch is split by
+    longest-processing-time packing of the sequences' compressed-key counts (strong
+    scaling; --scaling weak gives every rank its own batch) and the top-k ids are
+    all-gathered inside the step.  Returns the measurement as a dict (max over ranks)."""
     import torch
     import torch.distributed as dist
 
-    import unum_ops_b200
     from unum_ops_b200 import BlockSelectGraph, block_select
     from unum_ops_b200.sharding import plan_sequences, sequence_cost
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
-    unum_ops_b200.load()
+    steps = args.steps if steps is None else steps
+    warmup = args.warmup if warmup is None else warmup
     strong = args.scaling == "strong"
     B_all = args.decode_batch
     seed = 4 + (0 if strong else rank)
@@ -600,20 +612,20 @@ def run_decode(args):
         return out
 
     def timed(eager):
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             step(eager)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             step(eager)
         e1.record(stream)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
-        ms = e0.elapsed_time(e1) / args.steps
+        ms = e0.elapsed_time(e1) / steps
         if world > 1:
             t = torch.tensor([ms], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -625,23 +637,120 @@ def run_decode(args):
     # the graph replays the same kernels as the eager call: same top-k ids
     assert torch.equal(block_select(*sel_args, **sel_kw)[2], graph()[2])
     kbytes = int(k_lens.sum()) * HK * D * 2
+    hbm = load_peaks()[0]
+    seqs = B_all if strong else world * B_all
+    del graph
+    return {"ms_per_step": ms, "eager_ms_per_step": ms_eager, "sequences_per_s": seqs / (ms * 1e-3),
+            "sequences": seqs, "rank0_sequences": B, "shard_sizes": [len(p_) for p_ in plan],
+            "rank0_k_cmp_bytes": kbytes, "k_cmp_stream_gbs": kbytes / (ms * 1e-3) / 1e9,
+            "k_cmp_stream_frac": kbytes / (ms * 1e-3) / 1e9 / hbm,
+            "parallelism": (f"{world} ranks, sequences by LPT on compressed-key counts"
+                            if strong and world > 1 else f"dp{world}"),
+            "api": "BlockSelectGraph (block_select captured once in a CUDA graph, replayed per step)"}
+
+
+def measure_stage2(args, world, rank, dev, steps=20, warmup=3):
+    """The stage-2 consumer on the config-4 decode batch: each of the 512 tokens attends
+    (16 query heads per kv head) over its 64 selected 64-token blocks of a paged KV cache
+    (per-token block table [512, 65536] of random physical slots, 2^20 physical tokens),
+    the gather fused into the kernel (no slot tensor).  Sequences are split as in the
+    decode measurement.  HBM-bound: algorithmic bytes = K and V rows of the valid
+    positions + q + out + top-k ids + the table entries read."""
+    import torch
+    import torch.distributed as dist
+
+    from unum_ops_b200 import sparse_attention
+    from unum_ops_b200.sharding import plan_sequences, sequence_cost
+
+    strong = args.scaling == "strong"
+    B_all = args.decode_batch
+    rng = np.random.default_rng(40 + (0 if strong else rank))
+    ctx_all = rng.integers(4096, 65537, size=B_all)
+    if strong and world > 1:
+        plan = plan_sequences(sequence_cost([1] * B_all, (ctx_all - 32) // 16 + 1), world)
+    else:
+        plan = [list(range(B_all))] * world
+    mine = np.array(plan[rank], np.int64)
+    B = len(mine)
+    ctx = ctx_all[mine]
+    n_phys = 1 << 20
+    g = torch.Generator(device=dev).manual_seed(41 + rank)
+    table = torch.randint(0, n_phys, (B, 65536), generator=g, device=dev, dtype=torch.int32)
+    kc = torch.randn(n_phys * HK, D, generator=g, device=dev).to(torch.bfloat16)
+    vc = torch.randn(n_phys * HK, D, generator=g, device=dev).to(torch.bfloat16)
+    q = torch.randn(B, HQ, D, generator=g, device=dev).to(torch.bfloat16)
+    topk = np.empty((HK, B, TOPK), np.int32)
+    for h in range(HK):
+        for b in range(B):
+            nblk = (int(ctx[b]) + 63) // 64
+            topk[h, b] = np.sort(rng.choice(nblk, TOPK, replace=False))
+    topk_d = torch.from_numpy(topk).to(dev)
+    tb = torch.arange(B, dtype=torch.int32, device=dev)
+    pos = torch.from_numpy(ctx.astype(np.int32)).to(dev)
+    st = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def run():
+        return sparse_attention(q, kc, vc, topk_d, table, tb, pos, pos, status=st)
+
+    for _ in range(warmup):
+        run()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        run()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    if int(st.item()) != 0:
+        raise RuntimeError("stage-2 kernel reported a timeout")
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    valid = 0  # valid positions: p < ctx (the last selected block may be partial)
+    for b in range(B):
+        blocks = topk[:, b, :].astype(np.int64)
+        valid += int(np.minimum(64, np.maximum(0, int(ctx[b]) - blocks * 64)).sum())
+    nbytes = valid * D * 2 * 2 + B * HQ * D * 2 * 2 + topk.size * 4 + valid * 4
+    hbm = load_peaks()[0]
+    del kc, vc, table
+    return {"ms_per_step": ms, "kernel": "stage2_kernel (unum_sparse_attn_blocks)",
+            "tokens": B, "valid_positions": valid, "bytes": nbytes,
+            "gbs": nbytes / (ms * 1e-3) / 1e9, "frac": nbytes / (ms * 1e-3) / 1e9 / hbm, "bound": "hbm",
+            "workload": "C4 decode batch x top-64 blocks, paged KV cache (per-token table [B, 65536], "
+                        "2^20 physical tokens), 16 query heads per kv head"}
+
+
+def run_decode(args):
+    """--workload decode: the config-4 decode batch as the bench line itself."""
+    import torch
+    import torch.distributed as dist
+
+    import unum_ops_b200
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    unum_ops_b200.load()
+    d = measure_decode(args, world, rank, dev)
+    d["stage2"] = measure_stage2(args, world, rank, dev)
     if rank == 0:
-        hbm = load_peaks()[0]
-        seqs = B_all if strong else world * B_all
         emit({
-            "metric": f"decode block selection, sequences/s ({B_all} x 1 query, contexts U[4096,65536])",
-            "value": seqs / (ms * 1e-3), "unit": "sequences/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "strong" if strong else "weak",
+            "metric": f"decode block selection, sequences/s ({args.decode_batch} x 1 query, contexts U[4096,65536])",
+            "value": d["sequences_per_s"], "unit": "sequences/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": d["ms_per_step"],
+            "higher_is_better": True, "scaling": args.scaling,
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
-            "config": {"workload": "C4 decode batch",
-                       "parallelism": (f"{world} ranks, sequences by LPT on compressed-key counts"
-                                       if strong and world > 1 else f"dp{world}"),
-                       "rank0_sequences": B, "rank0_k_cmp_bytes": kbytes},
-            "api": "BlockSelectGraph (block_select captured once in a CUDA graph, replayed per step)",
-            "eager_ms_per_step": ms_eager,
-            "k_cmp_stream_gbs": kbytes / (ms * 1e-3) / 1e9,
-            "k_cmp_stream_frac": kbytes / (ms * 1e-3) / 1e9 / hbm})
+            "config": {"workload": "C4 decode batch", "parallelism": d["parallelism"]},
+            "decode": d})
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -773,7 +882,8 @@ def main():
     ap.add_argument("--seqlen", type=int, default=131072,
                     help="prefill length (default: the 128k headline workload)")
     ap.add_argument("--decode-batch", type=int, default=512,
-                    help="decode workload: sequences in the batch (config 4: 512)")
+                    help="decode batch (config 4: 512 sequences); the prefill line also carries "
+                         "its measurement under 'decode' (0: skip)")
     ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
                     help="N>1: strong = one sequence sharded by kv head x query range "
                          "(config 3); weak = every rank its own sequence")

@@ -114,7 +114,14 @@ def _exchange_worker(rank, world, port, ret):
     g, nh, a, b = shards[rank]
     full = torch.full((2, L, K), -7, dtype=torch.int32)
     sharding.exchange_shards(ref[g:g + nh, a:b].clone(), full, shards, rank)
-    ret.put((rank, bool(torch.equal(full, ref))))
+    ok = bool(torch.equal(full, ref))
+    # block ids on an int16 wire (ids < 2^15, -1 padding kept)
+    ids = (ref % 2048) - (ref % 7 == 0).to(torch.int32) * ((ref % 2048) + 1)
+    full2 = torch.full((2, L, K), -7, dtype=torch.int32)
+    wire = torch.empty((2, L, K), dtype=torch.int16)
+    sharding.exchange_shards(ids[g:g + nh, a:b].clone(), full2, shards, rank, wire=wire)
+    ok = ok and bool(torch.equal(full2, ids)) and bool((ids == -1).any())
+    ret.put((rank, ok))
     dist.barrier()
     dist.destroy_process_group()
 

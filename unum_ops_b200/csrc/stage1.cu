@@ -27,8 +27,7 @@
 //   warp 16    TMA producer (Q tile, 4-stage ring of K tiles)
 //   warp 17    TMEM allocator + single-thread UMMA issuer
 // The epilogue issues packed f32x2 FMA/ADD (half the instructions of scalar
-// code) and computes a share of its exponentials with a polynomial on the FMA
-// pipe, the rest on the MUFU pipe.
+// code) and takes its exponentials on the MUFU pipe (ex2.approx).
 // TMEM holds two 256-column accumulator buffers so the tensor core fills one
 // while the epilogue drains the other.
 //
@@ -133,52 +132,10 @@ __device__ __forceinline__ int32_t visible(int32_t lq, int32_t q_len, int32_t k_
     return off < 0 ? 0 : (off > k_len ? k_len : off);
 }
 
-// 2^x on the FMA pipe for two values at once, for a share of the
-// exponentials so the MUFU (ex2) pipe — 16 results per clock per SM — is not
-// the only unit doing them.  Split x = j + f with j = round(x) (adding
-// 1.5*2^23 rounds to an integer held in the low mantissa bits) and f in
-// [-0.5, 0.5]; 2^f by a cubic fitted to minimise the maximum relative error on
-// that interval (7.5e-5, far below the bf16 output precision); 2^j by adding
-// j to the exponent field (one integer multiply-add per value).  Inputs are
-// clamped to >= -126, so a score far below the row maximum yields about 2^-126
-// instead of a smaller number — negligible in any sum here.
-__device__ __forceinline__ uint64_t exp2_fma2(uint64_t x2) {
-    float lo, hi;
-    f2_unpack(x2, lo, hi);
-    x2 = f2_pack(fmaxf(lo, -126.0f), fmaxf(hi, -126.0f));
-    const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);
-    const uint64_t nmagic = f2_pack(-12582912.0f, -12582912.0f);
-    const uint64_t t = f2_add(x2, magic);                                   // 1.5*2^23 + j
-    const uint64_t f = f2_fma(f2_add(t, nmagic), f2_pack(-1.0f, -1.0f), x2);  // x - j
-    uint64_t p = f2_fma(f2_pack(0.055171460f, 0.055171460f), f, f2_pack(0.24261086f, 0.24261086f));
-    p = f2_fma(p, f, f2_pack(0.69326097f, 0.69326097f));
-    p = f2_fma(p, f, f2_pack(0.99992812f, 0.99992812f));
-    // bits(2^f) + (j << 23): the low 9 bits of bits(t) hold j (two's complement) and
-    // the magic's own bits shift out of the word
-    uint32_t rlo, rhi;
-    asm("mad.lo.u32 %0, %1, 8388608, %2;" : "=r"(rlo) : "r"((uint32_t)t), "r"((uint32_t)p));
-    asm("mad.lo.u32 %0, %1, 8388608, %2;" : "=r"(rhi) : "r"((uint32_t)(t >> 32)), "r"((uint32_t)(p >> 32)));
-    return (uint64_t)rlo | ((uint64_t)rhi << 32);
-}
-
 __device__ __forceinline__ uint64_t exp2_mufu2(uint64_t x2) {
     float lo, hi;
     f2_unpack(x2, lo, hi);
     return f2_pack(ex2(lo), ex2(hi));
-}
-
-// Pair p of a strip uses the polynomial when p % mod == mod-1 (mod 0: never);
-// pass 1 and pass 2 have their own share.
-#ifndef UNUM_POLY_MOD1
-#define UNUM_POLY_MOD1 0
-#endif
-#ifndef UNUM_POLY_MOD2
-#define UNUM_POLY_MOD2 0
-#endif
-template <int MOD, int P>
-__device__ __forceinline__ uint64_t exp2_pair_mod(uint64_t x2) {
-    if constexpr (MOD > 0 && P % (MOD > 0 ? MOD : 1) == MOD - 1) return exp2_fma2(x2);
-    else return exp2_mufu2(x2);
 }
 
 template <int QT>
@@ -213,21 +170,14 @@ struct Sync {
     int32_t *status;
 };
 
-#ifndef UNUM_WAIT_HINT_NS
-#define UNUM_WAIT_HINT_NS 0
-#endif
 // Bounded wait: false once this CTA has given up (then callers stop issuing work).
 __device__ __forceinline__ bool wait_bar(const Sync &s, uint32_t bar, uint32_t parity, int code) {
     if (*s.abort) return false;
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t_start = globaltimer_ns();
     for (uint32_t i = 1;; ++i) {
-#if UNUM_WAIT_HINT_NS > 0
-        if (mbar_try_wait_sleep(bar, parity, UNUM_WAIT_HINT_NS)) return true;
-#else
         if (mbar_try_wait(bar, parity)) return true;
-#endif
-        if ((i & (UNUM_WAIT_HINT_NS > 0 ? 3u : 63u)) == 0) {
+        if ((i & 63) == 0) {
             if (*s.abort) return false;
             if (globaltimer_ns() - t_start > kWaitNs) {
                 *s.abort = 1;
@@ -255,14 +205,7 @@ __device__ __forceinline__ void p1_chunk(float (&v)[N], int32_t colbase, int32_t
     if (mt == -INFINITY) return;
     const uint64_t nmc = f2_pack(-mt * c, -mt * c);
     uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
-#ifndef UNUM_P1_SCALAR
-#define UNUM_P1_SCALAR 0
-#endif
-#if UNUM_P1_SCALAR
-#define UNUM_P1(P) if ((P) < N / 2) { float lo_, hi_, e0_, e1_; f2_unpack(exp2_pair_mod<UNUM_POLY_MOD1, P>(f2_fma(f2_pack(v[2 * (P)], v[2 * (P) + 1]), c2, nmc)), e0_, e1_); f2_unpack(acc[(P) & 3], lo_, hi_); acc[(P) & 3] = f2_pack(lo_ + e0_, hi_ + e1_); }
-#else
-#define UNUM_P1(P) if ((P) < N / 2) acc[(P) & 3] = f2_add(acc[(P) & 3], exp2_pair_mod<UNUM_POLY_MOD1, P>(f2_fma(f2_pack(v[2 * (P)], v[2 * (P) + 1]), c2, nmc)));
-#endif
+#define UNUM_P1(P) if ((P) < N / 2) acc[(P) & 3] = f2_add(acc[(P) & 3], exp2_mufu2(f2_fma(f2_pack(v[2 * (P)], v[2 * (P) + 1]), c2, nmc)));
 #define UNUM_P1x4(P) UNUM_P1(P) UNUM_P1(P + 1) UNUM_P1(P + 2) UNUM_P1(P + 3)
     UNUM_P1x4(0) UNUM_P1x4(4) UNUM_P1x4(8) UNUM_P1x4(12)
     UNUM_P1x4(16) UNUM_P1x4(20) UNUM_P1x4(24) UNUM_P1x4(28)
@@ -276,14 +219,6 @@ __device__ __forceinline__ void p1_chunk(float (&v)[N], int32_t colbase, int32_t
     m = mt;
 }
 
-#ifndef UNUM_P2_SCALAR
-#define UNUM_P2_SCALAR 0
-#endif
-#if UNUM_P2_SCALAR
-#define UNUM_P2ACC(A, E) { float lo_, hi_, e0_, e1_; f2_unpack((E), e0_, e1_); f2_unpack((A), lo_, hi_); (A) = f2_pack(lo_ + e0_, hi_ + e1_); }
-#else
-#define UNUM_P2ACC(A, E) (A) = f2_add((A), (E));
-#endif
 // Pass 2 on accumulator columns H*32..H*32+31 of this warpgroup (key = TMEM lane):
 // add exp2(s*c - b) into the per-token head sums.
 template <int G, int H>
@@ -292,8 +227,8 @@ __device__ __forceinline__ void p2_chunk(const float (&v)[32], uint64_t (&acc)[6
 #define UNUM_P2(P, SV)                                                                              \
     {                                                                                               \
         const uint64_t x2 = f2_fma(f2_pack(v[2 * (P)], v[2 * (P) + 1]), c2, SV);                    \
-        const uint64_t e2 = exp2_pair_mod<UNUM_POLY_MOD2, H * 16 + (P)>(x2);                         \
-        UNUM_P2ACC(acc[(H * 32 + 2 * (P)) / G][(P) & 1], e2);                                         \
+        const uint64_t e2 = exp2_mufu2(x2);                         \
+        acc[(H * 32 + 2 * (P)) / G][(P) & 1] = f2_add(acc[(H * 32 + 2 * (P)) / G][(P) & 1], e2);                                         \
     }
 #define UNUM_P2x2(P)                                                                                \
     {                                                                                               \
@@ -549,11 +484,7 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(sy.s_empty + 8 * buf);  // values are in registers
-#ifndef UNUM_ABL_P1
                     p1_chunk<64>(v64, kt * kBN + colh, lim_r, c, c2, m, l);
-#else
-                    m = fmaxf(m, v64[kt & 63]);
-#endif
                 }
                 part[(wg & 1) * kRows + r] = make_float2(m, l);
                 named_bar_sync(kEpiBarrier, kEpiWarps * 32);
@@ -610,12 +541,8 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(sy.s_empty + 8 * buf);
-#ifndef UNUM_ABL_P2
                     p2_chunk<G, 0>(wa, acc, st4, c2);
                     p2_chunk<G, 1>(wb, acc, st4, c2);
-#else
-                    acc[0][0] = __float_as_uint(wa[kt & 31]);
-#endif
                     if (kTmaStore) {
                         // stage the warpgroup's [NQ tokens x 128 keys] tile in shared memory
                         const uint32_t buf_s = stc & 1;

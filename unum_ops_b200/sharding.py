@@ -91,7 +91,7 @@ def prefill_shard(world: int, rank: int, q_len: int, k_len: int, n_kv_heads: int
     return g, nh, a, b
 
 
-def exchange_shards(local, full, shards, rank, group=None):
+def exchange_shards(local, full, shards, rank, group=None, wire=None):
     """Gather every rank's shard of a [Hk, T, ...] result into ``full`` on every rank.
 
     ``shards[r] = (first kv head, kv heads, t_begin, t_end)`` of rank r (as from
@@ -99,18 +99,26 @@ def exchange_shards(local, full, shards, rank, group=None):
     Each rank sends its exact shard to every peer (point-to-point, no padding to the
     longest shard).  A one-head shard is a contiguous slice of ``full`` and is received
     in place; a shard of several heads arrives in a contiguous buffer and is copied in.
-    Works with any torch.distributed backend that has send/recv (NCCL on GPUs, gloo on
-    CPU)."""
+
+    ``wire``: an optional [Hk, T, ...] buffer of a narrower dtype (for example int16 for
+    block ids, which are below 2^15) that the shards travel in: the local shard is
+    narrowed into it, the peers' shards are received into it, and ``full`` is widened
+    from it once at the end, so half the bytes cross the links.  Values must fit the
+    narrower type.  Works with any torch.distributed backend that has send/recv (NCCL on
+    GPUs, gloo on CPU)."""
     import torch.distributed as dist
 
     g, nh, a, b = shards[rank]
-    full[g:g + nh, a:b].copy_(local)
-    send = local.contiguous()
+    tgt = full if wire is None else wire
+    tgt[g:g + nh, a:b].copy_(local)
+    send = tgt[g:g + nh, a:b]
+    if not send.is_contiguous():
+        send = send.contiguous()
     ops, staged = [], []
     for r, (gr, nhr, ar, br) in enumerate(shards):
         if r == rank:
             continue
-        dst = full[gr:gr + nhr, ar:br]
+        dst = tgt[gr:gr + nhr, ar:br]
         buf = dst if dst.is_contiguous() else torch.empty(dst.shape, dtype=dst.dtype, device=dst.device)
         if buf is not dst:
             staged.append((dst, buf))
@@ -121,4 +129,6 @@ def exchange_shards(local, full, shards, rank, group=None):
             w.wait()
     for dst, buf in staged:
         dst.copy_(buf)
+    if wire is not None:
+        full.copy_(wire)
     return full
