@@ -262,6 +262,34 @@ int unum_infllmv2_attn_stage1_noalloc(const void *q, int64_t T, int64_t Hq, int6
 int unum_stage1_noalloc_status(void *stream, int32_t *status_out);
 
 /*
+ * sparse_attn_blocks — stage-2 sparse attention over the selected blocks, the
+ * consumer of get_block_table with its gather fused in.  No reference function:
+ * the reference's get_block_table (get_table_torch.py:4-44) emits the slot ids
+ * such a kernel reads; here they are computed in the loader and never written.
+ *
+ *   q        bf16 [T, Hq, 128], strides (q_st, q_sh) elements, Hq = 16 * Hk
+ *   k_cache, v_cache  bf16 [n_slots, 128] contiguous rows; row = head_group *
+ *            physical token + kv head (get_block_table's slot numbering)
+ *   topk_idx int32 [Hk, T, K] (element strides ts_h, ts_t; k contiguous), K <= 64
+ *   block_table, token_to_bs, token_pos_in_bs, seqlen_q: as for unum_get_block_table
+ *   out      bf16 [T, Hq, 128] contiguous, fully written
+ *   status   optional device int32 (NULL: none): set to 0 on entry, nonzero when a
+ *            bounded wait inside the kernel gave up (output then invalid)
+ *
+ *   out[t,h] = sum_p softmax_p(q[t,h] . k_cache[slot_p] * softmax_scale) v_cache[slot_p]
+ *   over p = topk[g,t,k]*64 + i with topk >= 0, p < seqlen_q[bs], p < token_pos_in_bs[t],
+ *   slot_p = head_group * block_table[bs, min(p, L-1)] + g (g = h / 16, bs = token_to_bs[t]);
+ *   slots outside [0, n_slots) are skipped; 0 for a row with no valid position.
+ */
+int unum_sparse_attn_blocks(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, int64_t q_sh,
+                            const void *k_cache, const void *v_cache, int64_t n_slots, int64_t Hk,
+                            const int32_t *topk_idx, int64_t K, int64_t ts_h, int64_t ts_t,
+                            const int32_t *block_table, int64_t B, int64_t L, int64_t bt_stride,
+                            const int32_t *token_to_bs, const int32_t *token_pos_in_bs, int pos_is_scalar,
+                            const int32_t *seqlen_q, int seqlen_is_scalar, int32_t head_group,
+                            float softmax_scale, void *out, int32_t *status, void *stream);
+
+/*
  * compress_keys — the producer of stage 1's compressed keys (no reference
  * function: the reference's caller builds k_cmp; the layout is the one its
  * stage-1 kernel assumes, the 16-token stride of infllmv2_attn_stage1_triton_v2.py:70).

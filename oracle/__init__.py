@@ -56,6 +56,9 @@ def lib():
         L.oracle_get_block_table.restype = None
         L.oracle_compress_keys.argtypes = [_ptr, _i64, _ptr, _ptr, _i64, _i64, _i64, _ptr]
         L.oracle_compress_keys.restype = None
+        L.oracle_sparse_attn.argtypes = [_ptr, _i64, _i64, _i64, _ptr, _ptr, _i64, _i64, _ptr, _i64,
+                                         _ptr, _i64, _i64, _ptr, _ptr, _ptr, _i32, ctypes.c_float, _ptr]
+        L.oracle_sparse_attn.restype = None
         L.oracle_set_num_threads.argtypes = [ctypes.c_int]
         L.oracle_num_threads.restype = ctypes.c_int
         _lib = L
@@ -159,6 +162,32 @@ def get_block_table(topk_idx, block_table, token_to_bs, token_pos_in_bs, seqlen_
         lib().oracle_get_block_table(_p(tk), H, T, K, _p(bt), B, L, _p(tb), _p(pb),
                                      int(pb.size == 1), _p(sq), int(sq.size == 1),
                                      int(head_group), _p(out))
+    return out
+
+
+def sparse_attn(q, k_cache, v_cache, topk_idx, block_table, token_to_bs, token_pos_in_bs, seqlen_q,
+                head_group=2, softmax_scale=None):
+    """Stage-2 sparse attention over the selected blocks (oracle.c: oracle_sparse_attn):
+    q [T, Hq, D], k_cache / v_cache [n_slots, D] (slot = head_group * physical token + kv
+    head), topk_idx int32 [Hk, T, K]; returns float32 [T, Hq, D]."""
+    qf = _c(q, np.float32)
+    kc = _c(k_cache, np.float32).reshape(-1, qf.shape[-1])
+    vc = _c(v_cache, np.float32).reshape(-1, qf.shape[-1])
+    tk = _c(topk_idx, np.int32)
+    bt = _c(block_table, np.int32)
+    tb = _c(token_to_bs, np.int32)
+    T, Hq, D = qf.shape
+    pb = _c(np.broadcast_to(np.asarray(token_pos_in_bs, np.int32), (T,)), np.int32)
+    sq = _c(np.atleast_1d(seqlen_q), np.int32)
+    if sq.size == 1:
+        sq = np.full(bt.shape[0], sq[0], np.int32)
+    Hk, _, K = tk.shape
+    B, L = bt.shape
+    scale = D ** -0.5 if softmax_scale is None else softmax_scale
+    out = np.empty((T, Hq, D), np.float32)
+    if out.size:
+        lib().oracle_sparse_attn(_p(qf), T, Hq, D, _p(kc), _p(vc), kc.shape[0], Hk, _p(tk), K, _p(bt), B,
+                                 L, _p(tb), _p(pb), _p(sq), int(head_group), float(scale), _p(out))
     return out
 
 

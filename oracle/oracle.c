@@ -398,3 +398,88 @@ void oracle_compress_keys(const float *k, int64_t Hk, const int32_t *cu_in, cons
         }
     }
 }
+
+/* ------------------------------------------------------------------------ */
+/* Stage-2 sparse attention over the selected blocks: the consumer of       */
+/* get_block_table (no reference implementation; the definition follows the */
+/* slot rule of get_table_torch.py:29-44).  For token t, kv head g and each */
+/* query head h of the group g*G .. g*G+G-1:                                 */
+/*   positions p = topk[g,t,k]*64 + i (k < K, i < 64) with topk >= 0,        */
+/*   p < seqlen_q[bs] and p < token_pos_in_bs[t] (bs = token_to_bs[t]);       */
+/*   slot_p = head_group * block_table[bs, clamp(p, 0, L-1)] + g;             */
+/*   out[t,h] = sum_p softmax_p(q[t,h] . kc[slot_p] * scale) * vc[slot_p],    */
+/* in double accumulators, 0 when no position is valid.                      */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+    const float *q, *kc, *vc;
+    const int32_t *topk, *table, *tb, *pos, *seqlen;
+    int64_t T, Hq, Hk, D, K, L, n_slots;
+    int32_t head_group;
+    float scale;
+    float *out;
+} sattn_ctx;
+
+static void sattn_rows(int64_t rb, int64_t re, void *vctx) {
+    const sattn_ctx *c = (const sattn_ctx *)vctx;
+    const int64_t G = c->Hq / c->Hk, npos = c->K * 64;
+    int64_t *slot = (int64_t *)malloc(sizeof(int64_t) * (size_t)(npos > 0 ? npos : 1));
+    double *s = (double *)malloc(sizeof(double) * (size_t)(npos > 0 ? npos : 1));
+    double *acc = (double *)malloc(sizeof(double) * (size_t)c->D);
+    for (int64_t r = rb; r < re; ++r) {
+        const int64_t t = r / c->Hk, g = r % c->Hk;
+        const int64_t bs = c->tb[t];
+        int64_t n = 0;
+        for (int64_t k = 0; k < c->K; ++k) {
+            const int32_t blk = c->topk[(g * c->T + t) * c->K + k];
+            if (blk < 0) continue;
+            for (int64_t i = 0; i < 64; ++i) {
+                const int64_t p = (int64_t)blk * 64 + i;
+                if (p >= c->seqlen[bs] || p >= c->pos[t]) continue;
+                const int64_t col = p < 0 ? 0 : (p > c->L - 1 ? c->L - 1 : p);
+                const int64_t sl = (int64_t)c->head_group * c->table[bs * c->L + col] + g;
+                if (sl < 0 || sl >= c->n_slots) continue; /* outside the cache: not a valid key */
+                slot[n++] = sl;
+            }
+        }
+        for (int64_t hh = 0; hh < G; ++hh) {
+            const int64_t h = g * G + hh;
+            float *o = c->out + (t * c->Hq + h) * c->D;
+            const float *qr = c->q + (t * c->Hq + h) * c->D;
+            if (n == 0) {
+                for (int64_t d = 0; d < c->D; ++d) o[d] = 0.f;
+                continue;
+            }
+            double m = -INFINITY;
+            for (int64_t j = 0; j < n; ++j) {
+                const float *kr = c->kc + slot[j] * c->D;
+                double dot = 0.0;
+                for (int64_t d = 0; d < c->D; ++d) dot += (double)qr[d] * (double)kr[d];
+                s[j] = dot * (double)c->scale;
+                if (s[j] > m) m = s[j];
+            }
+            double l = 0.0;
+            for (int64_t d = 0; d < c->D; ++d) acc[d] = 0.0;
+            for (int64_t j = 0; j < n; ++j) {
+                const double e = exp(s[j] - m);
+                l += e;
+                const float *vr = c->vc + slot[j] * c->D;
+                for (int64_t d = 0; d < c->D; ++d) acc[d] += e * (double)vr[d];
+            }
+            for (int64_t d = 0; d < c->D; ++d) o[d] = (float)(acc[d] / l);
+        }
+    }
+    free(slot);
+    free(s);
+    free(acc);
+}
+
+void oracle_sparse_attn(const float *q, int64_t T, int64_t Hq, int64_t D, const float *kc,
+                        const float *vc, int64_t n_slots, int64_t Hk, const int32_t *topk, int64_t K,
+                        const int32_t *table, int64_t B, int64_t L, const int32_t *token_to_bs,
+                        const int32_t *pos_in_bs, const int32_t *seqlen, int32_t head_group,
+                        float scale, float *out) {
+    (void)B;
+    sattn_ctx c = {q, kc, vc, topk, table, token_to_bs, pos_in_bs, seqlen, T, Hq, Hk, D, K, L,
+                   n_slots, head_group, scale, out};
+    parallel_for(T * Hk, 8, sattn_rows, &c);
+}

@@ -51,6 +51,9 @@ SIGNATURES = {
                                           _i64, _p, _p, _i64, ctypes.c_float, _int, _p, _i64, _p,
                                           _i64, _i64, _i64, _i64, _i64, _p, ctypes.c_size_t, _p],
                                          _int),
+    "unum_sparse_attn_blocks": ([_p, _i64, _i64, _i64, _i64, _i64, _p, _p, _i64, _i64, _p, _i64, _i64, _i64,
+                                 _p, _i64, _i64, _i64, _p, _p, _int, _p, _int, _i32, ctypes.c_float, _p,
+                                 _p, _p], _int),
     "unum_infllmv2_attn_stage1_noalloc": ([_p, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64,
                                            _i64, _p, _p, _i64, ctypes.c_float, _int, _p, _i64, _p],
                                           _int),

@@ -162,6 +162,42 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 16 consecutive f32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ---------------------------------------------------------------- cp.async (gathers)
+// 16-byte asynchronous copy global -> shared; src_bytes 0 writes 16 zero bytes.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+
+// Arrive on `bar` once every cp.async this thread issued before has landed (the
+// barrier's expected count includes this thread).
+__device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// MN-major operand tile with 128-byte swizzle: rows along K of 64 bf16 along M/N
+// (128 bytes), 8-row groups `sbo` bytes apart along K, 64-element groups along
+// M/N `lbo` bytes apart.
+__device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
+}
+
 // K-major operand tile with 128-byte swizzle: rows of 64 bf16 (128 bytes),
 // 8-row core groups 1024 bytes apart.  `saddr` must sit in a 1024-byte
 // aligned tile (plus a multiple of 32 bytes to step along K).
@@ -173,6 +209,11 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
            ((uint32_t)(M >> 4) << 24);
+}
+
+// The same with the A operand MN-major.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32_amn(int M, int N) {
+    return idesc_bf16_f32(M, N) | (1u << 15);
 }
 
 __device__ __forceinline__ float ex2(float x) {
