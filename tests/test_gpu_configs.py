@@ -135,7 +135,12 @@ def test_c3_128k_prefill(dev, oracle_lib):
     torch.cuda.synchronize()
     W = scores.shape[-1]
     _row_sum_property(scores, cu_q, cu_k, 16)
-    for a in (0, 4096, 65536, L - 16):
+    # windows from the kernel's schedule as well as round numbers: work items are 16-token
+    # tiles dealt last-tile-first to the 148 persistent CTAs, so L-16 is the first item
+    # (most key tiles), L-75*16 the first CTA's second item (a persistent-CTA item
+    # boundary near the diagonal), and 129016 / 63*2048-8 straddle two tiles where the
+    # causal key count crosses a 128-key tile boundary (last key tile partly masked)
+    for a in (0, 4096, 65536, L - 16, L - 75 * 16, 129016, 63 * 2048 - 8):
         ref = _oracle_rows(oracle_lib, q, k, cu_q, cu_k, a, a + 16, W)
         np.testing.assert_allclose(scores[:, a:a + 16].float().cpu().numpy(), ref, atol=ATOL, rtol=RTOL)
     # downstream steps, exact, on sampled token ranges of the GPU's own outputs

@@ -66,10 +66,11 @@ constexpr uint32_t kOffQ = 0;                        // 2 Q slots
 constexpr uint32_t kOffKV = 2 * kSlotQ;              // 8 KB (1024-aligned)
 constexpr uint32_t kOffP = kOffKV + kStages * kStageKV;
 constexpr uint32_t kOffRed = kOffP + 2 * kStageP;
-constexpr uint32_t kOffBar = kOffRed + 2 * kEpiWarps * 32 * 4;
+constexpr uint32_t kOffSlots = kOffRed + 2 * kEpiWarps * 32 * 4;  // [2][32 tiles x 128 keys] int32
+constexpr uint32_t kOffBar = kOffSlots + 2 * kMaxTiles * kTileKeys * 4;
 // barriers: q_full[2], q_empty[2], kv_full[S], kv_empty[S], s_full, p_full[2], p_empty[2],
-// o_full, tmem_free
-constexpr uint32_t kNumBars = 4 + 2 * kStages + 1 + 4 + 2;
+// o_full, tmem_free, slot_full[2], slot_free[2]
+constexpr uint32_t kNumBars = 4 + 2 * kStages + 1 + 4 + 2 + 4;
 constexpr uint32_t kOffMisc = kOffBar + kNumBars * 8;
 constexpr uint32_t kSmemBytes = kOffMisc + 64 + 1024;
 static_assert(kOffKV % 1024 == 0 && kOffP % 1024 == 0, "SW128 tiles need 1024-byte alignment");
@@ -203,6 +204,8 @@ stage2_kernel(const __grid_constant__ Params p) {
     const uint32_t q_full = bar0, q_empty = bar0 + 16, kv_full = bar0 + 32, kv_empty = kv_full + 8 * kStages;
     const uint32_t s_full = kv_empty + 8 * kStages, p_full = s_full + 8, p_empty = p_full + 16;
     const uint32_t o_full = p_empty + 16, tmem_free = o_full + 8;
+    const uint32_t slot_full = tmem_free + 8, slot_free = slot_full + 16;
+    int32_t *slots_s = reinterpret_cast<int32_t *>(sgen + kOffSlots);  // [2][kMaxTiles * 128]
     volatile int *abort_flag = reinterpret_cast<volatile int *>(sgen + kOffMisc);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sgen + kOffMisc + 16);
     float *red = reinterpret_cast<float *>(sgen + kOffRed);
@@ -215,6 +218,8 @@ stage2_kernel(const __grid_constant__ Params p) {
             mbar_init(q_empty + 8 * i, 1);
             mbar_init(p_full + 8 * i, 4);  // the 4 epilogue warps that write a tile's P
             mbar_init(p_empty + 8 * i, 1);
+            mbar_init(slot_full + 8 * i, kLoadWarps * 32);
+            mbar_init(slot_free + 8 * i, kEpiWarps);
         }
         for (int s = 0; s < kStages; ++s) {
             mbar_init(kv_full + 8 * s, kLoadWarps * 32);
@@ -253,12 +258,20 @@ stage2_kernel(const __grid_constant__ Params p) {
                 cp_async16(qdst + (ch >> 3) * kPanelQ + h * 128 + (((ch & 7) ^ (h & 7)) << 4), src, 16);
             }
             cp_async_arrive(q_full + 8 * qs);
+            // the slot of key j of every tile, all looked up at once (independent loads) and
+            // kept in shared memory for the gathers and the epilogue's masks
+            if (!wait_bar(sy, slot_free + 8 * qs, ((qn >> 1) & 1) ^ 1, 40)) break;
+            int32_t *my_slots = slots_s + qs * (kMaxTiles * kTileKeys);
+#pragma unroll
+            for (int32_t i = 0; i < kMaxTiles; ++i)
+                if (i < it.nt) my_slots[i * kTileKeys + j] = (int32_t)key_slot(p, it.t, it.g, i, j, it.bs, it.lim);
+            mbar_arrive(slot_full + 8 * qs);
             for (int phase = 0; phase < 2; ++phase) {
                 const __nv_bfloat16 *cache = phase == 0 ? p.kc : p.vc;
                 for (int32_t i = 0; i < it.nt; ++i, ++kc_cnt) {
                     const uint32_t s = kc_cnt % kStages;
                     if (!wait_bar(sy, kv_empty + 8 * s, ((kc_cnt / kStages) & 1) ^ 1, 42)) break;
-                    const int64_t slot = key_slot(p, it.t, it.g, i, j, it.bs, it.lim);
+                    const int64_t slot = my_slots[i * kTileKeys + j];
                     const __nv_bfloat16 *src = cache + (slot < 0 ? 0 : slot) * kD;
                     const uint32_t dst = sbase + kOffKV + s * kStageKV + j * 128;
 #pragma unroll
@@ -338,8 +351,10 @@ stage2_kernel(const __grid_constant__ Params p) {
         for (int64_t w = blockIdx.x; w < n_items; w += gridDim.x, ++qn) {
             const ItemInfo it = item_info(p, w);
             const bool bad = !wait_bar(sy, s_full, qn & 1, 48);
-            if (named_bar_or(kEpiBar, kEpiWarps * 32, bad)) break;  // gave up: all epilogue warps leave
+            const bool bad1 = !wait_bar(sy, slot_full + 8 * (qn & 1), (qn >> 1) & 1, 51);
+            if (named_bar_or(kEpiBar, kEpiWarps * 32, bad || bad1)) break;  // gave up: all epilogue warps leave
             tc_fence_after();
+            const int32_t *islots = slots_s + (qn & 1) * (kMaxTiles * kTileKeys);
             float m[kG], l[kG];
 #pragma unroll
             for (int h = 0; h < kG; ++h) {
@@ -348,7 +363,7 @@ stage2_kernel(const __grid_constant__ Params p) {
             }
             // read 1: per-head maximum over this thread's keys
             for (int32_t i = par; i < it.nt; i += 2) {
-                const bool valid = key_slot(p, it.t, it.g, i, key, it.bs, it.lim) >= 0;
+                const bool valid = islots[i * kTileKeys + key] >= 0;
                 float v[kG];
                 tmem_ld16(tmem + lane_base + i * kG, v);  // warp-collective: every lane loads
                 tmem_wait_ld();
@@ -360,7 +375,7 @@ stage2_kernel(const __grid_constant__ Params p) {
             reduce16<true>(m, red, ew, lane);
             // read 2: per-head sum of exp2((s - max) * c)
             for (int32_t i = par; i < it.nt; i += 2) {
-                const bool valid = key_slot(p, it.t, it.g, i, key, it.bs, it.lim) >= 0;
+                const bool valid = islots[i * kTileKeys + key] >= 0;
                 float v[kG];
                 tmem_ld16(tmem + lane_base + i * kG, v);
                 tmem_wait_ld();
@@ -379,7 +394,7 @@ stage2_kernel(const __grid_constant__ Params p) {
                 const uint32_t ps = pc & 1;
                 const bool bad2 = !wait_bar(sy, p_empty + 8 * ps, ((pc >> 1) & 1) ^ 1, 49);
                 if (__any_sync(0xffffffffu, bad2)) break;
-                const bool valid = key_slot(p, it.t, it.g, i, key, it.bs, it.lim) >= 0;
+                const bool valid = islots[i * kTileKeys + key] >= 0;
                 float v[kG];
                 tmem_ld16(tmem + lane_base + i * kG, v);
                 tmem_wait_ld();
@@ -413,6 +428,8 @@ stage2_kernel(const __grid_constant__ Params p) {
                 __syncwarp();
                 if (lane == 0) mbar_arrive(tmem_free);
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(slot_free + 8 * (qn & 1));  // this item's masks are no longer read
         }
     }
 
