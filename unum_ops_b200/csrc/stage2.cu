@@ -15,9 +15,12 @@
 // (0 when no position is valid).
 //
 // One work item = (token, kv head): up to K*64 = 4096 keys in 128-key tiles.
-//   phase 1  the loader warps gather the item's key rows (cp.async, 16-byte
-//            chunks written in the 128-byte-swizzled UMMA layout, invalid
-//            positions zero-filled) and the MMA warp computes S^T = K Q^T per
+//   phase 1  the loader warps look up the item's slots once (shared memory),
+//            then one thread gathers the key rows with TMA row gathers
+//            (tile::gather4: four rows of one 64-column panel per instruction,
+//            written in the 128-byte-swizzled UMMA layout; an invalid position
+//            reads a row past the cache, which TMA fills with zeros), and the
+//            MMA warp computes S^T = K Q^T per
 //            tile (M = 128 keys, N = 16 heads) into its own 16 TMEM columns, so
 //            all of the item's scores stay in tensor memory (32 tiles x 16 = 512
 //            columns);
@@ -35,6 +38,7 @@
 // status in `status` (if given), stops issuing work, drains and returns.
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cudaTypedefs.h>
 
 #include "common.cuh"
 #include "sm100.cuh"
@@ -43,11 +47,23 @@ namespace {
 
 using namespace unum::sm100;
 
+// TMA gather of four rows (y0..y3) of a 2-D tensor, columns x..x+63, into four
+// consecutive 128-byte rows of shared memory (128-byte swizzle), completion
+// counted on `bar`.  No multicast.
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const void *tmap, int32_t x, int32_t y0, int32_t y1,
+                                            int32_t y2, int32_t y3, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(bar)
+        : "memory");
+}
+
 constexpr int kD = 128;
 constexpr int kG = 16;               // query heads per kv head
 constexpr int kTileKeys = 128;
 constexpr int kMaxTiles = 32;        // K <= 64 blocks of 64 positions
-constexpr int kStages = 4;           // key/value tile ring
+constexpr int kStages = 5;           // key/value tile ring
 constexpr int kLoadWarps = 4;        // one loader thread per key of a tile
 constexpr int kEpiWarps = 8;         // two per TMEM lane quarter, alternating tiles
 constexpr int kEpi0 = kLoadWarps;    // first epilogue warp
@@ -195,7 +211,8 @@ __device__ __forceinline__ void reduce16(float (&v)[kG], float *red, int ew, int
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-stage2_kernel(const __grid_constant__ Params p) {
+stage2_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+              const __grid_constant__ Params p) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t sbase = (raw + 1023u) & ~1023u;
@@ -222,7 +239,7 @@ stage2_kernel(const __grid_constant__ Params p) {
             mbar_init(slot_free + 8 * i, kEpiWarps);
         }
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(kv_full + 8 * s, kLoadWarps * 32);
+            mbar_init(kv_full + 8 * s, 64);  // the 64 gathering threads' expect_tx
             mbar_init(kv_empty + 8 * s, 1);
         }
         mbar_init(s_full, 1);
@@ -249,7 +266,11 @@ stage2_kernel(const __grid_constant__ Params p) {
             const ItemInfo it = item_info(p, w);
             // the token's 16 query heads: 256 chunks of 16 bytes, two per thread
             const uint32_t qs = qn & 1;
-            if (!wait_bar(sy, q_empty + 8 * qs, ((qn >> 1) & 1) ^ 1, 41)) break;
+            // both buffers of this item free, decided by all loader threads together (a
+            // thread leaving alone would strand the others at the named barrier below)
+            bool bad = !wait_bar(sy, q_empty + 8 * qs, ((qn >> 1) & 1) ^ 1, 41);
+            bad = !wait_bar(sy, slot_free + 8 * qs, ((qn >> 1) & 1) ^ 1, 40) || bad;
+            if (named_bar_or(2, kLoadWarps * 32, bad)) break;
             const uint32_t qdst = sbase + kOffQ + qs * kSlotQ;
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
@@ -260,29 +281,32 @@ stage2_kernel(const __grid_constant__ Params p) {
             cp_async_arrive(q_full + 8 * qs);
             // the slot of key j of every tile, all looked up at once (independent loads) and
             // kept in shared memory for the gathers and the epilogue's masks
-            if (!wait_bar(sy, slot_free + 8 * qs, ((qn >> 1) & 1) ^ 1, 40)) break;
             int32_t *my_slots = slots_s + qs * (kMaxTiles * kTileKeys);
 #pragma unroll
             for (int32_t i = 0; i < kMaxTiles; ++i)
                 if (i < it.nt) my_slots[i * kTileKeys + j] = (int32_t)key_slot(p, it.t, it.g, i, j, it.bs, it.lim);
             mbar_arrive(slot_full + 8 * qs);
-            for (int phase = 0; phase < 2; ++phase) {
-                const __nv_bfloat16 *cache = phase == 0 ? p.kc : p.vc;
-                for (int32_t i = 0; i < it.nt; ++i, ++kc_cnt) {
-                    const uint32_t s = kc_cnt % kStages;
-                    if (!wait_bar(sy, kv_empty + 8 * s, ((kc_cnt / kStages) & 1) ^ 1, 42)) break;
-                    const int64_t slot = my_slots[i * kTileKeys + j];
-                    const __nv_bfloat16 *src = cache + (slot < 0 ? 0 : slot) * kD;
-                    const uint32_t dst = sbase + kOffKV + s * kStageKV + j * 128;
-#pragma unroll
-                    for (int ch = 0; ch < 16; ++ch)
-                        cp_async16(dst + (ch >> 3) * kPanelKV + (((ch & 7) ^ (j & 7)) << 4), src + ch * 8,
-                                   slot < 0 ? 0u : 16u);
-                    cp_async_arrive(kv_full + 8 * s);
+            named_bar_sync(2, kLoadWarps * 32);  // every slot of the item is in shared memory
+            if (j < 64) {
+                // threads 0..63 each gather four rows (row quad j % 32) of one panel (j / 32)
+                const int rq = j & 31, panel = j >> 5;
+                const int32_t oob = (int32_t)p.n_slots;  // a row past the cache: read as zeros
+                for (int phase = 0; phase < 2; ++phase) {
+                    const void *tm = phase == 0 ? (const void *)&tmK : (const void *)&tmV;
+                    for (int32_t i = 0; i < it.nt; ++i, ++kc_cnt) {
+                        const uint32_t s = kc_cnt % kStages;
+                        if (!wait_bar(sy, kv_empty + 8 * s, ((kc_cnt / kStages) & 1) ^ 1, 42)) continue;
+                        const int4 r = reinterpret_cast<const int4 *>(my_slots + i * kTileKeys)[rq];
+                        const int32_t y0 = r.x < 0 ? oob : r.x, y1 = r.y < 0 ? oob : r.y;
+                        const int32_t y2 = r.z < 0 ? oob : r.z, y3 = r.w < 0 ? oob : r.w;
+                        mbar_arrive_expect_tx(kv_full + 8 * s, 4 * 128);
+                        tma_gather4(sbase + kOffKV + s * kStageKV + panel * kPanelKV + rq * 512, tm, 64 * panel,
+                                    y0, y1, y2, y3, kv_full + 8 * s);
+                    }
                 }
-                if (*abort_flag) break;
+            } else {
+                kc_cnt += 2 * (uint32_t)it.nt;
             }
-            if (*abort_flag) break;
         }
         asm volatile("cp.async.wait_all;" ::: "memory");
     } else if (warp == kMmaWarp) {
@@ -447,6 +471,40 @@ stage2_kernel(const __grid_constant__ Params p) {
     }
 }
 
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+    return fn;
+}
+
+// [n_slots, 128] bf16 rows, 256-byte row stride, gathered one 64-column panel x one
+// row per box (the box of a tile::gather4 load is one row high), 128-byte swizzle.
+int make_rows_map(CUtensorMap *m, const void *base, int64_t n_slots) {
+    auto enc = encode_fn();
+    if (!enc) {
+        unum::set_error("cuTensorMapEncodeTiled unavailable from the driver");
+        return UNUM_ERR_CUDA;
+    }
+    cuuint64_t gdim[2] = {(cuuint64_t)kD, (cuuint64_t)n_slots};
+    cuuint64_t gstride[1] = {(cuuint64_t)kD * 2};
+    cuuint32_t box[2] = {64, 1};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), gdim, gstride, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        unum::set_error("cuTensorMapEncodeTiled (kv cache) failed (%d)", (int)r);
+        return UNUM_ERR_CUDA;
+    }
+    return UNUM_OK;
+}
+
 }  // namespace
 
 extern "C" int unum_sparse_attn_blocks(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st,
@@ -499,6 +557,10 @@ extern "C" int unum_sparse_attn_blocks(const void *q, int64_t T, int64_t Hq, int
     p.c = softmax_scale * kLog2e;
     p.out = (__nv_bfloat16 *)out;
     p.status = status;
+    UNUM_CHECK_ARG(n_slots > 0 && n_slots < ((int64_t)1 << 31), "n_slots must be in [1, 2^31)");
+    CUtensorMap mk, mv;
+    if (int rc = make_rows_map(&mk, k_cache, n_slots)) return rc;
+    if (int rc = make_rows_map(&mv, v_cache, n_slots)) return rc;
     cudaStream_t s = (cudaStream_t)stream;
     if (status) UNUM_CHECK_CUDA(cudaMemsetAsync(status, 0, sizeof(int32_t), s));
     UNUM_CHECK_CUDA(cudaFuncSetAttribute(stage2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -506,6 +568,6 @@ extern "C" int unum_sparse_attn_blocks(const void *q, int64_t T, int64_t Hq, int
     const int64_t items = T * Hk;
     const int64_t sms = unum::sm_count();
     const int grid = (int)(items < sms ? items : sms);
-    stage2_kernel<<<grid, kThreads, kSmemBytes, s>>>(p);
+    stage2_kernel<<<grid, kThreads, kSmemBytes, s>>>(mk, mv, p);
     return unum::check_launch("stage2_kernel");
 }
