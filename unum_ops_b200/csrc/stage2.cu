@@ -260,17 +260,17 @@ stage2_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ C
 
     if (warp < kLoadWarps) {
         // ---------------------------------------------------------------- loaders
-        const int j = threadIdx.x;  // key of every tile this thread gathers; 0..127
-        uint32_t kc_cnt = 0, qn = 0;
-        for (int64_t w = blockIdx.x; w < n_items; w += gridDim.x, ++qn) {
+        const int j = threadIdx.x;  // 0..127
+        uint32_t kc_cnt = 0;
+        // q and the slots of item w into buffer qn & 1; false when a wait gave up (decided by
+        // all loader threads together: one leaving alone would strand the others at a barrier)
+        auto prepare = [&](int64_t w, uint32_t qn) -> bool {
             const ItemInfo it = item_info(p, w);
-            // the token's 16 query heads: 256 chunks of 16 bytes, two per thread
             const uint32_t qs = qn & 1;
-            // both buffers of this item free, decided by all loader threads together (a
-            // thread leaving alone would strand the others at the named barrier below)
             bool bad = !wait_bar(sy, q_empty + 8 * qs, ((qn >> 1) & 1) ^ 1, 41);
             bad = !wait_bar(sy, slot_free + 8 * qs, ((qn >> 1) & 1) ^ 1, 40) || bad;
-            if (named_bar_or(2, kLoadWarps * 32, bad)) break;
+            if (named_bar_or(2, kLoadWarps * 32, bad)) return false;
+            // the token's 16 query heads: 256 chunks of 16 bytes, two per thread
             const uint32_t qdst = sbase + kOffQ + qs * kSlotQ;
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
@@ -287,25 +287,41 @@ stage2_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ C
                 if (i < it.nt) my_slots[i * kTileKeys + j] = (int32_t)key_slot(p, it.t, it.g, i, j, it.bs, it.lim);
             mbar_arrive(slot_full + 8 * qs);
             named_bar_sync(2, kLoadWarps * 32);  // every slot of the item is in shared memory
-            if (j < 64) {
-                // threads 0..63 each gather four rows (row quad j % 32) of one panel (j / 32)
-                const int rq = j & 31, panel = j >> 5;
-                const int32_t oob = (int32_t)p.n_slots;  // a row past the cache: read as zeros
-                for (int phase = 0; phase < 2; ++phase) {
-                    const void *tm = phase == 0 ? (const void *)&tmK : (const void *)&tmV;
-                    for (int32_t i = 0; i < it.nt; ++i, ++kc_cnt) {
-                        const uint32_t s = kc_cnt % kStages;
-                        if (!wait_bar(sy, kv_empty + 8 * s, ((kc_cnt / kStages) & 1) ^ 1, 42)) continue;
-                        const int4 r = reinterpret_cast<const int4 *>(my_slots + i * kTileKeys)[rq];
-                        const int32_t y0 = r.x < 0 ? oob : r.x, y1 = r.y < 0 ? oob : r.y;
-                        const int32_t y2 = r.z < 0 ? oob : r.z, y3 = r.w < 0 ? oob : r.w;
-                        mbar_arrive_expect_tx(kv_full + 8 * s, 4 * 128);
-                        tma_gather4(sbase + kOffKV + s * kStageKV + panel * kPanelKV + rq * 512, tm, 64 * panel,
-                                    y0, y1, y2, y3, kv_full + 8 * s);
-                    }
-                }
-            } else {
-                kc_cnt += 2 * (uint32_t)it.nt;
+            return true;
+        };
+        // the key (phase 0) or value (phase 1) tiles of an item: threads 0..63 each gather four
+        // rows (row quad j % 32) of one panel (j / 32) per tile
+        auto gather = [&](const ItemInfo &it, uint32_t qs, int phase) {
+            if (j >= 64) {
+                kc_cnt += (uint32_t)it.nt;
+                return;
+            }
+            const int rq = j & 31, panel = j >> 5;
+            const int32_t oob = (int32_t)p.n_slots;  // a row past the cache: read as zeros
+            const int32_t *my_slots = slots_s + qs * (kMaxTiles * kTileKeys);
+            const void *tm = phase == 0 ? (const void *)&tmK : (const void *)&tmV;
+            for (int32_t i = 0; i < it.nt; ++i, ++kc_cnt) {
+                const uint32_t s = kc_cnt % kStages;
+                if (!wait_bar(sy, kv_empty + 8 * s, ((kc_cnt / kStages) & 1) ^ 1, 42)) continue;
+                const int4 r = reinterpret_cast<const int4 *>(my_slots + i * kTileKeys)[rq];
+                const int32_t y0 = r.x < 0 ? oob : r.x, y1 = r.y < 0 ? oob : r.y;
+                const int32_t y2 = r.z < 0 ? oob : r.z, y3 = r.w < 0 ? oob : r.w;
+                mbar_arrive_expect_tx(kv_full + 8 * s, 4 * 128);
+                tma_gather4(sbase + kOffKV + s * kStageKV + panel * kPanelKV + rq * 512, tm, 64 * panel, y0, y1,
+                            y2, y3, kv_full + 8 * s);
+            }
+        };
+        // item n's keys, then the next item's q and slots (their lookups overlap item n's
+        // softmax), then item n's values
+        uint32_t qn = 0;
+        int64_t w = blockIdx.x;
+        if (w < n_items && prepare(w, 0)) {
+            for (; w < n_items; w += gridDim.x, ++qn) {
+                const ItemInfo it = item_info(p, w);
+                gather(it, qn & 1, 0);
+                const bool ok = w + gridDim.x >= n_items || prepare(w + gridDim.x, qn + 1);
+                gather(it, qn & 1, 1);
+                if (!ok) break;
             }
         }
         asm volatile("cp.async.wait_all;" ::: "memory");
