@@ -726,7 +726,7 @@ extern "C" int unum_topk_blocks(const void *scores, int dtype, int64_t rows, int
         UNUM_CHECK_CUDA(cudaMemsetAsync(out, 0xff, (size_t)rows * K * sizeof(int32_t), s));
         return UNUM_OK;
     }
-    if ((dtype == UNUM_DTYPE_BF16 || dtype == UNUM_DTYPE_F16) && !getenv("UNUM_TOPK_OLD"))
+    if ((dtype == UNUM_DTYPE_BF16 || dtype == UNUM_DTYPE_F16) && getenv("UNUM_TOPK_NEW"))
         return unum_topk16_launch(scores, dtype, rows, NB, row_stride, K, out, s);
     switch (dtype) {
         case UNUM_DTYPE_F32: return launch_topk<float>(scores, rows, NB, row_stride, K, out, s);
