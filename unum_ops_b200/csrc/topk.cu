@@ -23,13 +23,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
-#include <cstdlib>
-
 #include "common.cuh"
-
-// 16-bit score rows (topk16.cu)
-int unum_topk16_launch(const void *scores, int dtype, int64_t rows, int64_t NB, int64_t row_stride, int64_t K,
-                       int32_t *out, cudaStream_t s);
 
 namespace {
 
@@ -726,8 +720,6 @@ extern "C" int unum_topk_blocks(const void *scores, int dtype, int64_t rows, int
         UNUM_CHECK_CUDA(cudaMemsetAsync(out, 0xff, (size_t)rows * K * sizeof(int32_t), s));
         return UNUM_OK;
     }
-    if ((dtype == UNUM_DTYPE_BF16 || dtype == UNUM_DTYPE_F16) && getenv("UNUM_TOPK_NEW"))
-        return unum_topk16_launch(scores, dtype, rows, NB, row_stride, K, out, s);
     switch (dtype) {
         case UNUM_DTYPE_F32: return launch_topk<float>(scores, rows, NB, row_stride, K, out, s);
         case UNUM_DTYPE_BF16: return launch_topk<__nv_bfloat16>(scores, rows, NB, row_stride, K, out, s);

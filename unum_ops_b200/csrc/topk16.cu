@@ -9,7 +9,8 @@
 // pooled rows are close, so the previous row's K-th key is a good hint.  The row
 // is loaded once with coalesced 16-byte loads and staged in shared memory; lane
 // l then owns the contiguous chunk [l*C, l*C + C) (C = padded NB / 32), so one
-// warp scan of per-lane counts keeps block order.  Per row:
+// warp scan of per-lane counts keeps block order (the staging pads each chunk
+// by 16 bytes so that the lanes' chunk reads are free of bank conflicts).  Per row:
 //   1. with a hint kp, every score is compared (packed bf16x2 / half2 compares)
 //      with the bound t = kp - margin; when between K and kCap pass, their keys
 //      go to a candidate list and one 256-bin histogram of (key - t) (bins
@@ -126,15 +127,16 @@ topk16_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t ro
     const int32_t NBp = (NB + 255) & ~255;  // padded: C = NBp/32 is a multiple of 8
     const int32_t C = NBp >> 5;
     const int32_t nvec = C >> 3;
-    uint8_t *wb = smem + (size_t)warp * (1024 + kCap * 4 + (size_t)NBp * 2);
+    // the staged row: lane l's chunk at 16-byte slots l*(nvec+1) .. (one slot of padding per
+    // chunk, so the lanes' reads of their chunks hit distinct banks)
+    uint8_t *wb = smem + (size_t)warp * (1024 + kCap * 4 + (size_t)NBp * 2 + 512);
     uint32_t *hist = reinterpret_cast<uint32_t *>(wb);
     uint32_t *cand = reinterpret_cast<uint32_t *>(wb + 1024);             // candidate keys
     uint16_t *rowb = reinterpret_cast<uint16_t *>(wb + 1024 + kCap * 4);  // the row's bits
-    const uint16_t *chunk = rowb + lane * C;
+    const uint16_t *chunk = rowb + lane * (C + 8);
     const int64_t gw = (int64_t)blockIdx.x * kWarps + warp;
     const int64_t r0 = gw * rows_per_warp;
     const int64_t r1 = r0 + rows_per_warp < rows ? r0 + rows_per_warp : rows;
-    const uint32_t lt_mask = (1u << lane) - 1u;
     uint32_t hint = 0;     // K-th key of the previous row (0: none)
     uint32_t margin = 16;  // key steps below the hint
     for (int64_t row = r0; row < r1; ++row) {
@@ -164,19 +166,46 @@ topk16_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t ro
             }
 #pragma unroll
             for (int j = 0; j < 8; ++j)
-                if (v0 + j < nvec) *reinterpret_cast<uint4 *>(rowb + 8 * ((v0 + j) * 32 + lane)) = w[j];
+                if (v0 + j < nvec) {
+                    const int32_t g = (v0 + j) * 32 + lane;  // global vector: chunk g / nvec, slot g % nvec
+                    *reinterpret_cast<uint4 *>(rowb + 8 * (g + g / nvec)) = w[j];
+                }
         }
         __syncwarp();
         uint32_t kth = 0;   // K-th largest key; 0 with take_all
         bool take_all = false, found = false;
         if (hint != 0u) {
             // ---- 1. candidates >= t = hint - margin
-            const uint32_t t = hint > Tr<T>::kMinKey + margin ? hint - margin : Tr<T>::kMinKey;
+            // a bound that misses (fewer than K or more than kCap above it) is moved and
+            // retried a few times, bracketing the K-th key, before the bitwise search
+            uint32_t t = hint > Tr<T>::kMinKey + margin ? hint - margin : Tr<T>::kMinKey;
+            uint32_t t_few = 0u, t_many = 0u;  // bounds seen with too few / too many above
             uint32_t bm[4];
-            chunk_mask<T, Cmp::Ge>(chunk, nvec, bits2_of_key(t), bm);
-            uint32_t n;
-            uint32_t slot = excl_scan(popc4(bm), lane, n);
-            if (n >= (uint32_t)K && n <= (uint32_t)kCap) {
+            uint32_t n = 0, slot = 0;
+            bool ok = false;
+#pragma unroll 1
+            for (int attempt = 0; attempt < 5; ++attempt) {
+                chunk_mask<T, Cmp::Ge>(chunk, nvec, bits2_of_key(t), bm);
+                slot = excl_scan(popc4(bm), lane, n);
+                if (n >= (uint32_t)K && n <= (uint32_t)kCap) {
+                    ok = true;
+                    break;
+                }
+                if (n < (uint32_t)K) {
+                    t_few = t;
+                    if (t <= Tr<T>::kMinKey) break;  // fewer than K candidates in all
+                    const uint32_t lo = t_many ? t_many : (t > Tr<T>::kMinKey + 4 * margin ? t - 4 * margin
+                                                                                          : Tr<T>::kMinKey);
+                    t = t_many ? (t_many + t) / 2 : lo;
+                    if (attempt == 0) margin = margin < 512u ? margin * 4 : 512u;
+                } else {
+                    t_many = t;
+                    t = t_few ? (t + t_few + 1) / 2 : min(t + margin, Tr<T>::kMaxKey);
+                    if (attempt == 0) margin = margin > 1u ? margin / 2 : 1u;
+                }
+                if (t_few && t_many && t_few <= t_many + 1) break;  // adjacent keys: a run of ties
+            }
+            if (ok) {
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
                     for (uint32_t m = bm[q]; m != 0u; m &= m - 1u)
@@ -221,10 +250,6 @@ topk16_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t ro
                     found = true;
                 }
                 if (n > (uint32_t)kCap / 2) margin = margin > 1u ? margin / 2 : 1u;
-            } else if (n < (uint32_t)K) {
-                margin = margin < 512u ? margin * 4 : 512u;
-            } else {
-                margin = margin > 1u ? margin / 2 : 1u;
             }
             __syncwarp();
         }
@@ -289,7 +314,7 @@ template <typename T>
 int launch(const void *scores, int64_t rows, int64_t NB, int64_t row_stride, int64_t K, int32_t *out,
            cudaStream_t s) {
     const int64_t NBp = (NB + 255) / 256 * 256;
-    const size_t smem = (size_t)kWarps * (1024 + kCap * 4 + (size_t)NBp * 2);
+    const size_t smem = (size_t)kWarps * (1024 + kCap * 4 + (size_t)NBp * 2 + 512);
     auto kern = topk16_kernel<T>;
     UNUM_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int per_sm = 0;  // one resident wave; runs of consecutive rows per warp reuse the hint
