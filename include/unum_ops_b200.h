@@ -184,7 +184,9 @@ int unum_infllmv2_attn_stage1(const void *q, int64_t T, int64_t Hq, int64_t D, i
  * must cover every sequence's compressed keys (max_seqlen_k >= each
  * cu_seqlens_k difference — the reference kernel writes past its rows
  * otherwise); with a smaller out_stride the pooled result may differ from the
- * separate pooling call, which then reads neighbouring rows.
+ * separate pooling call, which then reads neighbouring rows.  `out` may be
+ * NULL: the scores then stay on chip and only `pooled` is written (for a caller
+ * that needs the selection and not the scores).
  */
 int unum_infllmv2_attn_stage1_pooled(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st,
                                      int64_t q_sh, const void *k, int64_t Tk, int64_t Hk,
@@ -204,7 +206,8 @@ int unum_infllmv2_attn_stage1_pooled(const void *q, int64_t T, int64_t Hq, int64
  * overlapping the host-to-device copy of the next chunk's queries), with the
  * same results as one full call when the chunks cover all tokens.  Tiles are
  * 256/G tokens of one sequence counted from the sequence start; a window edge
- * inside a tile computes (and rewrites) the whole tile.
+ * inside a tile computes (and rewrites) the whole tile.  `out` may be NULL when
+ * `pooled` is given (scores kept on chip).
  */
 int unum_infllmv2_attn_stage1_window(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st,
                                      int64_t q_sh, const void *k, int64_t Tk, int64_t Hk,

@@ -569,6 +569,32 @@ def test_stage1_forced_expiry_drains_and_recovers(path, dev, oracle_lib, monkeyp
     np.testing.assert_allclose(out.float().cpu().numpy(), orc, atol=ATOL, rtol=RTOL)
 
 
+def test_block_select_without_scores_matches(dev):
+    """block_select(return_scores=False): the stage-1 scores stay on chip; pooled blocks,
+    top-k ids and slots are identical to the call that writes the scores."""
+    from unum_ops_b200 import block_select
+
+    rng = np.random.default_rng(12)
+    q_lens = np.array([3000, 17, 1200], np.int64)
+    k_lens = np.array([(n - 32) // 16 + 1 if n >= 32 else 1 for n in q_lens], np.int64)
+    T, Tk = int(q_lens.sum()), int(k_lens.sum())
+    q = _t(rng.standard_normal((T, 32, 128), dtype=np.float32), dev, torch.bfloat16)
+    k = _t(rng.standard_normal((Tk, 2, 128), dtype=np.float32), dev, torch.bfloat16)
+    cu_q, cu_k = _t(cases.cu(q_lens), dev), _t(cases.cu(k_lens), dev)
+    table = _t(rng.permutation(3 * 4096).astype(np.int32).reshape(3, 4096), dev)
+    tb = _t(np.repeat(np.arange(3, dtype=np.int32), q_lens), dev)
+    pos = _t(np.concatenate([np.arange(1, n + 1) for n in q_lens]).astype(np.int32), dev)
+    sl = _t(q_lens.astype(np.int32), dev)
+    args = (q, k, cu_q, cu_k, int(k_lens.max()), table, tb, pos, sl)
+    full = block_select(*args, max_context_len=4096)
+    part = block_select(*args, max_context_len=4096, return_scores=False)
+    torch.cuda.synchronize()
+    assert part[0] is None
+    for a, b in zip(full[1:], part[1:]):
+        assert torch.equal(a.view(torch.int16) if a.dtype == torch.bfloat16 else a,
+                           b.view(torch.int16) if b.dtype == torch.bfloat16 else b)
+
+
 def test_block_select_graph_replays_new_inputs(dev):
     """BlockSelectGraph: a replay after writing new values into the static inputs gives
     what the eager block_select gives on those values (decode-shaped batch)."""

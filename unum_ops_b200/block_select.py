@@ -20,13 +20,14 @@ __all__ = ["topk_blocks", "block_select", "BlockSelectGraph", "block_select_rows
 
 
 def stage1_pooled(q, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_k, max_context_len,
-                  local_blocks, init_blocks, causal=True, softmax_scale=None):
+                  local_blocks, init_blocks, causal=True, softmax_scale=None, write_scores=True):
     """Stage 1 and block max-pooling in one kernel launch.
 
     Returns (scores, pooled), identical to
     ``infllmv2_attn_stage1(...)`` followed by ``max_pooling_1d_varlen(scores, cu_q, cu_k,
     zeros, 16 * W, max_context_len, local_blocks, init_blocks)`` with W the scores' row
-    length.  Needs n_heads / n_kv_heads >= 16."""
+    length.  Needs n_heads / n_kv_heads >= 16.  With ``write_scores=False`` the scores
+    stay on chip (returned as None) and only the pooled blocks reach memory."""
     dev = _lib.require_cuda(q, k_cmp, cu_seqlens_q, cu_seqlens_k)
     q = (q if q.stride(-1) == 1 else q.contiguous()).to(torch.bfloat16)
     k = (k_cmp if k_cmp.stride(-1) == 1 else k_cmp.contiguous()).to(torch.bfloat16)
@@ -38,18 +39,18 @@ def stage1_pooled(q, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_k, max_contex
     cu_q, cu_k = _as_i32(cu_seqlens_q), _as_i32(cu_seqlens_k)
     W = _round_multiple(int(max_seqlen_k), 128)
     NB = math.ceil(max_context_len / 64)
-    scores = torch.empty(Hk, T, W, dtype=torch.bfloat16, device=dev)
+    scores = torch.empty(Hk, T, W, dtype=torch.bfloat16, device=dev) if write_scores else None
     pooled = torch.empty(Hk, T, NB, dtype=torch.bfloat16, device=dev)
     if T == 0 or W == 0 or NB == 0:
-        return scores.zero_(), pooled
+        return (scores.zero_() if scores is not None else None), pooled
     L = _lib.load()
     ws = _workspace(dev, int(L.unum_stage1_workspace_size(B)))
     with torch.cuda.device(dev):
         rc = L.unum_infllmv2_attn_stage1_pooled(
             q.data_ptr(), T, Hq, D, q.stride(0), q.stride(1), k.data_ptr(), Tk, Hk, k.stride(0),
             k.stride(1), cu_q.data_ptr(), cu_k.data_ptr(), B, float(softmax_scale), int(bool(causal)),
-            scores.data_ptr(), W, pooled.data_ptr(), NB, int(init_blocks), int(local_blocks),
-            ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
+            scores.data_ptr() if scores is not None else None, W, pooled.data_ptr(), NB, int(init_blocks),
+            int(local_blocks), ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
     _lib.check(rc)
     return scores, pooled
 
@@ -83,7 +84,7 @@ def topk_blocks(scores: torch.Tensor, topk: int) -> torch.Tensor:
 def block_select(q, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_k, block_table, token_to_bs,
                  token_pos_in_bs, seqlen_q, *, max_context_len, cache_lens=None, causal=True,
                  init_blocks=1, local_blocks=2, topk=64, block_size=64, stride=16,
-                 softmax_scale=None):
+                 softmax_scale=None, return_scores=True):
     """Run the whole block-selection path; returns (scores, pooled, topk_idx, slots).
 
     scores  bf16 [Hk, T, W]     stage-1 output, W = round_up(max_seqlen_k, 128)
@@ -92,6 +93,8 @@ def block_select(q, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_k, block_table
     slots   int32 [T, Hk, topk*64]  physical slot ids (get_block_table_ref_torch semantics)
     The pooling step reads stage-1 rows with flat stride W, i.e. it is called
     with max_seqlen_q = stride * W (the glue the reference's caller applies).
+    ``return_scores=False``: on the fused path (G >= 16, no cache) the stage-1 scores are
+    never written to memory and None is returned in their place.
     """
     G = q.shape[1] // k_cmp.shape[1]
     if (cache_lens is None and block_size == 64 and stride == 16 and G >= 16 and k_cmp.shape[0] > 0
@@ -99,7 +102,7 @@ def block_select(q, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_k, block_table
         # one launch: the pooling is taken from the scores while they are on chip
         scores, pooled = stage1_pooled(q, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_k,
                                        max_context_len, local_blocks, init_blocks, causal,
-                                       softmax_scale)
+                                       softmax_scale, write_scores=return_scores)
     else:
         scores = infllmv2_attn_stage1(q, k_cmp, None, cu_seqlens_q, cu_seqlens_k,
                                       max_seqlen_k=max_seqlen_k, causal=causal,
@@ -182,7 +185,7 @@ def block_select_rows(q, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_k, block_
     W = _round_multiple(int(max_seqlen_k), 128)
     NB = math.ceil(max_context_len / 64)
     n = t_end - t_begin
-    scores = torch.empty(Hk, T, W, dtype=torch.bfloat16, device=dev)
+    scores = torch.empty(Hk, T, W, dtype=torch.bfloat16, device=dev) if write_scores else None
     pooled = torch.empty(Hk, T, NB, dtype=torch.bfloat16, device=dev)
     idx = torch.empty(Hk, n, topk, dtype=torch.int32, device=dev)
     slots = torch.empty(n, Hk, topk * 64, dtype=torch.int32, device=dev)
@@ -251,7 +254,7 @@ def block_select_streamed(q_host, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_
     W = _round_multiple(int(max_seqlen_k), 128)
     NB = math.ceil(max_context_len / 64)
     q = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=dev)
-    scores = torch.empty(Hk, T, W, dtype=torch.bfloat16, device=dev)
+    scores = torch.empty(Hk, T, W, dtype=torch.bfloat16, device=dev) if write_scores else None
     pooled = torch.empty(Hk, T, NB, dtype=torch.bfloat16, device=dev)
     idx = torch.empty(Hk, n, topk, dtype=torch.int32, device=dev)
     slots = torch.empty(n, Hk, topk * 64, dtype=torch.int32, device=dev)

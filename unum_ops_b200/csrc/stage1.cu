@@ -256,7 +256,7 @@ __device__ __noinline__ void fill_tails(const Params &p, const int32_t *cu_tiles
         const int32_t c0 = it.nkt * kBN;
         const int32_t n16 = (int32_t)((p.out_stride - c0) >> 3);  // 16-byte chunks a row
         const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
-        for (int32_t tq = 0; tq < it.nq && n16 > 0; ++tq) {
+        for (int32_t tq = 0; p.out != nullptr && tq < it.nq && n16 > 0; ++tq) {
             uint4 *dst = reinterpret_cast<uint4 *>(
                 p.out + ((int64_t)it.g * p.T + it.t0 + tq) * p.out_stride + c0);
             for (int32_t e = lane; e < n16; e += 32) __stcs(dst + e, z4);
@@ -561,7 +561,9 @@ stage1_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                         if (wq == 0 && lane == 0) bulk_wait_read_all();  // previous store left its buffer
                         named_bar_sync(2 + wg, 128);
                         const int t_idx = wq * 32 + lane;
-                        if (tq0 + NQ <= it.nq) {  // whole tile belongs to this sequence: one TMA store
+                        if (p.out == nullptr) {
+                            // scores not wanted (pooling only): nothing leaves the staging tile
+                        } else if (tq0 + NQ <= it.nq) {  // whole tile belongs to this sequence: one TMA store
                             if (t_idx == 0) {
                                 tma_store_2d(&tmO, smem_u32(stg), kt * kBN,
                                              (int32_t)((int64_t)it.g * p.T + it.t0 + tq0));
@@ -720,8 +722,10 @@ stage1_prologue(const int32_t *__restrict__ cu_q, int32_t n_seq, int32_t QT, int
                 t = hi - 1;
                 continue;
             }
-            uint4 *row = reinterpret_cast<uint4 *>(out + ((int64_t)g * T + t) * out_stride);
-            for (int64_t e = tid; e < per_row; e += 1024) row[e] = make_uint4(0, 0, 0, 0);
+            if (out) {
+                uint4 *row = reinterpret_cast<uint4 *>(out + ((int64_t)g * T + t) * out_stride);
+                for (int64_t e = tid; e < per_row; e += 1024) row[e] = make_uint4(0, 0, 0, 0);
+            }
             if (pooled) {  // no sequence: k_len 0, local block 0 (max_pooling_1d_varlen.py:69-80)
                 __nv_bfloat16 *prow = pooled + ((int64_t)g * T + t) * NB;
                 for (int32_t j = tid; j < NB; j += 1024) {
@@ -1269,7 +1273,7 @@ int stage1_run(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, in
         return UNUM_ERR_UNSUPPORTED;
     }
     UNUM_CHECK_ARG(out_stride % 128 == 0, "out_stride must be a multiple of 128");
-    UNUM_CHECK_ARG(q && out && cu_seqlens_q && cu_seqlens_k, "null pointer argument");
+    UNUM_CHECK_ARG(q && (out || pooled) && cu_seqlens_q && cu_seqlens_k, "null pointer argument");
     UNUM_CHECK_ARG(unum::aligned16(out), "out must be 16-byte aligned");
     UNUM_CHECK_ARG(T < (int64_t)1 << 31 && Tk < (int64_t)1 << 31, "too many tokens");
     if (!workspace || workspace_bytes < unum_stage1_workspace_size(n_seq)) {
@@ -1293,7 +1297,7 @@ int stage1_run(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, in
         unum::set_error("fused pooling needs at least one compressed key");
         return UNUM_ERR_UNSUPPORTED;
     }
-    if (Tk == 0) {  // no compressed keys anywhere: every row is zero
+    if (Tk == 0 && out) {  // no compressed keys anywhere: every row is zero
         UNUM_CHECK_CUDA(cudaMemsetAsync(out, 0, (size_t)Hk * T * out_stride * 2, s));
         return UNUM_OK;
     }
@@ -1337,7 +1341,8 @@ int stage1_run(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, in
         return G == 16 ? launch_decode<16>(mqd, mk, p, s) : launch_decode<32>(mqd, mk, p, s);
     }
     CUtensorMap mo;  // out as a 2-D [Hk*T, out_stride] bf16 tensor, [64/G x 128] store boxes
-    {
+    memset(&mo, 0, sizeof(mo));
+    if (out) {
         auto enc = get_encode_fn();
         cuuint64_t gdim[2] = {(cuuint64_t)out_stride, (cuuint64_t)(Hk * T)};
         cuuint64_t gstride[1] = {(cuuint64_t)out_stride * 2};
