@@ -91,6 +91,12 @@ def prefill_shard(world: int, rank: int, q_len: int, k_len: int, n_kv_heads: int
     return g, nh, a, b
 
 
+def _as_sendable(t):
+    """The same bytes as a dtype every backend transports: NCCL in torch rejects int16, so
+    16-bit integer buffers travel reinterpreted as float16 (send/recv copy bytes only)."""
+    return t.view(torch.float16) if t.dtype in (torch.int16, torch.uint16) else t
+
+
 def exchange_shards(local, full, shards, rank, group=None, wire=None):
     """Gather every rank's shard of a [Hk, T, ...] result into ``full`` on every rank.
 
@@ -122,8 +128,8 @@ def exchange_shards(local, full, shards, rank, group=None, wire=None):
         buf = dst if dst.is_contiguous() else torch.empty(dst.shape, dtype=dst.dtype, device=dst.device)
         if buf is not dst:
             staged.append((dst, buf))
-        ops.append(dist.P2POp(dist.isend, send, r, group=group))
-        ops.append(dist.P2POp(dist.irecv, buf, r, group=group))
+        ops.append(dist.P2POp(dist.isend, _as_sendable(send), r, group=group))
+        ops.append(dist.P2POp(dist.irecv, _as_sendable(buf), r, group=group))
     if ops:
         for w in dist.batch_isend_irecv(ops):
             w.wait()
