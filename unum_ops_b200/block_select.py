@@ -185,7 +185,7 @@ def block_select_rows(q, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_k, block_
     W = _round_multiple(int(max_seqlen_k), 128)
     NB = math.ceil(max_context_len / 64)
     n = t_end - t_begin
-    scores = torch.empty(Hk, T, W, dtype=torch.bfloat16, device=dev) if write_scores else None
+    scores = torch.empty(Hk, T, W, dtype=torch.bfloat16, device=dev)
     pooled = torch.empty(Hk, T, NB, dtype=torch.bfloat16, device=dev)
     idx = torch.empty(Hk, n, topk, dtype=torch.int32, device=dev)
     slots = torch.empty(n, Hk, topk * 64, dtype=torch.int32, device=dev)
@@ -254,7 +254,7 @@ def block_select_streamed(q_host, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_
     W = _round_multiple(int(max_seqlen_k), 128)
     NB = math.ceil(max_context_len / 64)
     q = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=dev)
-    scores = torch.empty(Hk, T, W, dtype=torch.bfloat16, device=dev) if write_scores else None
+    scores = torch.empty(Hk, T, W, dtype=torch.bfloat16, device=dev)
     pooled = torch.empty(Hk, T, NB, dtype=torch.bfloat16, device=dev)
     idx = torch.empty(Hk, n, topk, dtype=torch.int32, device=dev)
     slots = torch.empty(n, Hk, topk * 64, dtype=torch.int32, device=dev)
