@@ -573,8 +573,8 @@ def measure_decode(args, world, rank, dev, steps=None, warmup=None):
     """512 sequences x 1 query token, contexts U[4096, 65536].  A step is
     block_select on the batch (one CUDA-graph replay).  With N ranks the batch is split by
     longest-processing-time packing of the sequences' compressed-key counts (strong
-    scaling; --scaling weak gives every rank its own batch) and the top-k ids are
-    all-gathered inside the step.  Returns the measurement as a dict (max over ranks)."""
+    scaling; --scaling weak gives every rank its own batch); a rank's ids and slots stay
+    on that rank (no exchange step: the sequences are independent).  Returns the measurement as a dict (max over ranks)."""
     import torch
     import torch.distributed as dist
 
@@ -613,20 +613,15 @@ def measure_decode(args, world, rank, dev, steps=None, warmup=None):
     pos = torch.from_numpy(ctx.astype(np.int32)).to(dev)
     cache = torch.from_numpy((ctx - 1).astype(np.int32)).to(dev)
     stream = torch.cuda.current_stream(dev)
-    pad = max(len(p) for p in plan)
-    gather_src = torch.zeros(HK, pad, TOPK, dtype=torch.int32, device=dev)
-    gather_dst = torch.empty(world, HK, pad, TOPK, dtype=torch.int32, device=dev)
 
     sel_args = (q, k, cu_q, cu_k, int(k_lens.max()), table, tb, pos, pos)
     sel_kw = dict(max_context_len=65536, cache_lens=cache)
     graph = BlockSelectGraph(*sel_args, **sel_kw)  # the decode loop's form: one graph replay
 
     def step(eager=False):
-        out = block_select(*sel_args, **sel_kw) if eager else graph()
-        if world > 1:
-            gather_src[:, :B].copy_(out[2])
-            dist.all_gather_into_tensor(gather_dst, gather_src)
-        return out
+        # no collective: decode sequences are independent, and each rank keeps its own
+        # sequences' ids and slots, which its own stage 2 consumes
+        return block_select(*sel_args, **sel_kw) if eager else graph()
 
     def timed(eager):
         for _ in range(warmup):
@@ -663,7 +658,8 @@ def measure_decode(args, world, rank, dev, steps=None, warmup=None):
             "k_cmp_stream_frac": kbytes / (ms * 1e-3) / 1e9 / hbm,
             "parallelism": (f"{world} ranks, sequences by LPT on compressed-key counts"
                             if strong and world > 1 else f"dp{world}"),
-            "api": "BlockSelectGraph (block_select captured once in a CUDA graph, replayed per step)"}
+            "api": ("BlockSelectGraph (block_select captured once in a CUDA graph, replayed per step): "
+                    "the fused decode kernel (stage 1, pooling, top-k, get_block_table in one launch)")}
 
 
 def measure_stage2(args, world, rank, dev, steps=20, warmup=3):

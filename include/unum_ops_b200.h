@@ -198,6 +198,42 @@ int unum_infllmv2_attn_stage1_pooled(const void *q, int64_t T, int64_t Hq, int64
                                      size_t workspace_bytes, void *stream);
 
 /*
+ * block_select_decode — the whole selection path of a decode batch in one launch:
+ * stage 1 (the decode kernel: one CTA per (token, kv head) at a time, the token's
+ * score row whole in tensor memory), then, from that row on chip, the block
+ * max-pooling, the top-K and get_block_table.  No single reference function:
+ * bit-identical to unum_infllmv2_attn_stage1 (out, row stride out_stride),
+ * then max_pooling_1d_varlen (max_pooling_1d_varlen.py:127-183: block_size 64,
+ * stride 16, max_seqlen_q = 16 * out_stride, cache_lens, NB, local_blocks,
+ * init_blocks), then unum_topk_blocks (K), then unum_get_block_table
+ * (get_table_torch.py:4-44 with the given head_group) — what block_select
+ * runs as four kernels over HBM.
+ *   out       bf16 [Hk, T, out_stride] scores, or NULL (kept on chip)
+ *   pooled    bf16 [Hk, T, NB] block scores, or NULL
+ *   topk_idx  int32 [Hk, T, K] (required)
+ *   slots     int32 [T, Hk, K*64] physical slot ids, or NULL (then the block-table
+ *             arguments are ignored)
+ *   cache_lens int32 [n_seq], or NULL for zeros
+ * Returns UNUM_ERR_UNSUPPORTED (nothing launched) unless G = Hq/Hk is 16 or 32,
+ * D = 128, n_seq >= 1, Tk >= 1, out_stride <= 128*512/G, 0 < NB with
+ * 4*NB <= out_stride (every pooling window inside the row) and 0 < K <= 1024.
+ * Any T is accepted; the kernel takes one work item per (token, kv head), so it
+ * is the fast path when sequences have one or a few query tokens.  Workspace and
+ * status word as for unum_infllmv2_attn_stage1 (unum_stage1_status).
+ */
+int unum_block_select_decode(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st,
+                             int64_t q_sh, const void *k, int64_t Tk, int64_t Hk, int64_t k_st,
+                             int64_t k_sh, const int32_t *cu_seqlens_q, const int32_t *cu_seqlens_k,
+                             const int32_t *cache_lens, int64_t n_seq, float softmax_scale,
+                             int causal, void *out, int64_t out_stride, void *pooled, int64_t NB,
+                             int64_t init_blocks, int64_t local_blocks, int32_t *topk_idx, int64_t K,
+                             int32_t *slots, const int32_t *block_table, int64_t B, int64_t L,
+                             int64_t bt_stride, const int32_t *token_to_bs,
+                             const int32_t *token_pos_in_bs, int pos_is_scalar,
+                             const int32_t *seqlen_q, int seqlen_is_scalar, int32_t head_group,
+                             void *workspace, size_t workspace_bytes, void *stream);
+
+/*
  * infllmv2_attn_stage1_window — stage 1 (optionally with fused pooling, pooled
  * may be NULL) restricted to a window of tokens: only query tiles whose tokens
  * intersect [t_begin, t_end) are computed and written; other rows of `out`

@@ -47,6 +47,10 @@ SIGNATURES = {
     "unum_infllmv2_attn_stage1_pooled": ([_p, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64,
                                           _i64, _p, _p, _i64, ctypes.c_float, _int, _p, _i64, _p,
                                           _i64, _i64, _i64, _p, ctypes.c_size_t, _p], _int),
+    "unum_block_select_decode": ([_p, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p, _p, _p,
+                                  _i64, ctypes.c_float, _int, _p, _i64, _p, _i64, _i64, _i64, _p, _i64,
+                                  _p, _p, _i64, _i64, _i64, _p, _p, _int, _p, _int, _i32, _p,
+                                  ctypes.c_size_t, _p], _int),
     "unum_infllmv2_attn_stage1_window": ([_p, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64,
                                           _i64, _p, _p, _i64, ctypes.c_float, _int, _p, _i64, _p,
                                           _i64, _i64, _i64, _i64, _i64, _p, ctypes.c_size_t, _p],

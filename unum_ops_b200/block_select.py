@@ -97,6 +97,10 @@ def block_select(q, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_k, block_table
     never written to memory and None is returned in their place.
     """
     G = q.shape[1] // k_cmp.shape[1]
+    if _decode_fusable(q, k_cmp, cu_seqlens_q, max_seqlen_k, max_context_len, topk, block_size, stride):
+        return _block_select_decode(q, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_k, block_table,
+                                    token_to_bs, token_pos_in_bs, seqlen_q, max_context_len, cache_lens,
+                                    causal, init_blocks, local_blocks, topk, softmax_scale, return_scores)
     if (cache_lens is None and block_size == 64 and stride == 16 and G >= 16 and k_cmp.shape[0] > 0
             and q.shape[-1] == 128):
         # one launch: the pooling is taken from the scores while they are on chip
@@ -115,6 +119,63 @@ def block_select(q, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_k, block_table
                                        stride)
     idx = topk_blocks(pooled, topk)
     slots = get_block_table_ref_torch(idx, block_table, token_to_bs, token_pos_in_bs, seqlen_q)
+    return scores, pooled, idx, slots
+
+
+def _decode_fusable(q, k_cmp, cu_seqlens_q, max_seqlen_k, max_context_len, topk, block_size, stride):
+    """Whether block_select can run as one fused decode launch: one or a few query
+    tokens per sequence, a head group of 16 or 32, each token's score row within tensor
+    memory (W <= 128 * 512 / G) and every pooling window inside the row (4 * NB <= W)."""
+    T, Hq, D = q.shape
+    Hk = k_cmp.shape[1]
+    n_seq = cu_seqlens_q.numel() - 1
+    if Hk == 0 or Hq % Hk or Hq // Hk not in (16, 32) or D != 128 or block_size != 64 or stride != 16:
+        return False
+    if T == 0 or n_seq <= 0 or k_cmp.shape[0] == 0 or T > 4 * n_seq:
+        return False
+    W = _round_multiple(int(max_seqlen_k), 128)
+    NB = math.ceil(max_context_len / block_size)
+    return 0 < NB and 4 * NB <= W <= 128 * 512 // (Hq // Hk) and 0 < topk <= 1024
+
+
+def _block_select_decode(q, k_cmp, cu_seqlens_q, cu_seqlens_k, max_seqlen_k, block_table, token_to_bs,
+                         token_pos_in_bs, seqlen_q, max_context_len, cache_lens, causal, init_blocks,
+                         local_blocks, topk, softmax_scale, return_scores):
+    """block_select as one launch (unum_block_select_decode): the decode kernel pools, selects
+    and maps each token's row while it is on chip.  Same results as the four-kernel chain."""
+    dev = _lib.require_cuda(q, k_cmp, cu_seqlens_q, cu_seqlens_k, block_table, token_to_bs,
+                            token_pos_in_bs, seqlen_q)
+    q = (q if q.stride(-1) == 1 else q.contiguous()).to(torch.bfloat16)
+    k = (k_cmp if k_cmp.stride(-1) == 1 else k_cmp.contiguous()).to(torch.bfloat16)
+    if softmax_scale is None:
+        softmax_scale = q.shape[-1] ** (-0.5)
+    T, Hq, D = q.shape
+    Tk, Hk = k.shape[0], k.shape[1]
+    B = cu_seqlens_q.numel() - 1
+    cu_q, cu_k = _as_i32(cu_seqlens_q), _as_i32(cu_seqlens_k)
+    cache = _as_i32(cache_lens) if cache_lens is not None else None
+    W = _round_multiple(int(max_seqlen_k), 128)
+    NB = math.ceil(max_context_len / 64)
+    scores = torch.empty(Hk, T, W, dtype=torch.bfloat16, device=dev) if return_scores else None
+    pooled = torch.empty(Hk, T, NB, dtype=torch.bfloat16, device=dev)
+    idx = torch.empty(Hk, T, topk, dtype=torch.int32, device=dev)
+    slots = torch.empty(T, Hk, topk * 64, dtype=torch.int32, device=dev)
+    bt = block_table if block_table.dtype == torch.int32 else block_table.to(torch.int32)
+    if bt.stride(1) != 1:
+        bt = bt.contiguous()
+    tb, pos, sq = _as_i32(token_to_bs), _as_i32(token_pos_in_bs), _as_i32(seqlen_q)
+    L = _lib.load()
+    ws = _workspace(dev, int(L.unum_stage1_workspace_size(B)))
+    with torch.cuda.device(dev):
+        rc = L.unum_block_select_decode(
+            q.data_ptr(), T, Hq, D, q.stride(0), q.stride(1), k.data_ptr(), Tk, Hk, k.stride(0),
+            k.stride(1), cu_q.data_ptr(), cu_k.data_ptr(), cache.data_ptr() if cache is not None else None,
+            B, float(softmax_scale), int(bool(causal)), scores.data_ptr() if scores is not None else None,
+            W, pooled.data_ptr(), NB, int(init_blocks), int(local_blocks), idx.data_ptr(), topk,
+            slots.data_ptr(), bt.data_ptr(), bt.shape[0], bt.shape[1], bt.stride(0), tb.data_ptr(),
+            pos.data_ptr(), int(pos.numel() == 1), sq.data_ptr(), int(sq.numel() == 1), 2,
+            ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
+    _lib.check(rc)
     return scores, pooled, idx, slots
 
 

@@ -19,6 +19,9 @@ constexpr int kGbtUnroll = 4;
 // tk: the row's K block ids (stride ts_k); trow: the sequence's block-table row
 // (L entries); orow: the row's K*64 output ids (16-byte aligned).  Writes the row's
 // int4 items [e_begin, e_end) (of K*16; e_begin a multiple of 32*kGbtUnroll).
+// kIdsWritten: tk was written by the calling kernel (shared memory, say), so it is
+// read with plain loads rather than through the read-only cache.
+template <bool kIdsWritten = false>
 __device__ __forceinline__ void gbt_emit_row(const int32_t *__restrict__ tk, int64_t ts_k, int32_t K,
                                              const int32_t *__restrict__ trow, int32_t lim, int32_t L,
                                              uint32_t head_group, uint32_t h, bool vec_ok,
@@ -32,7 +35,8 @@ __device__ __forceinline__ void gbt_emit_row(const int32_t *__restrict__ tk, int
 #pragma unroll
         for (int u = 0; u < kGbtUnroll; ++u) {
             const int32_t e = e0 + u * 32 + lane;
-            const int32_t idx = e < items ? __ldg(tk + (int64_t)(e >> 4) * ts_k) : -1;
+            const int32_t *ip = tk + (int64_t)(e >> 4) * ts_k;
+            const int32_t idx = e < items ? (kIdsWritten ? *ip : __ldg(ip)) : -1;
             p0[u] = (int32_t)((uint32_t)idx * (uint32_t)kGbtBlock + (uint32_t)q4);
         }
         int4 v[kGbtUnroll];

@@ -43,6 +43,7 @@
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
+#include "gbt_row.cuh"
 #include "sm100.cuh"
 
 namespace {
@@ -823,6 +824,36 @@ constexpr uint32_t kDecSmemBytes = kDecOffMisc + 64 + 1024;
 static_assert(kDecOffK % 1024 == 0 && kDecQSlot % 1024 == 0, "SW128 operand tiles need 1024-byte alignment");
 static_assert(kDecSmemBytes <= 232448, "exceeds the 227 KB of shared memory a CTA may use");
 
+// Fused selection (unum_block_select_decode): a decode item's whole score row sits in
+// one CTA, so the epilogue also pools it into 64-token blocks, picks the top-K blocks
+// and writes their physical slot ids, the steps block_select otherwise runs as three
+// more kernels over HBM.  Scratch: the row's bf16 scores, two 256-bin histograms, the
+// selected ids and a few scan words.
+struct DecSel {
+    const int32_t *cache_lens;  // [n_seq] added to the pooling's key count, or null (0)
+    __nv_bfloat16 *pooled;      // [Hk, T, NB] or null
+    int32_t *topk;              // [Hk, T, K]
+    int32_t *slots;             // [T, Hk, K*64] or null
+    const int32_t *table;       // block table [B, L], row stride bt_stride
+    const int32_t *tok_bs, *tok_pos, *seqlen;
+    int64_t bt_stride;
+    int32_t B, L, pos_scalar, seqlen_scalar;
+    uint32_t head_group;
+    int32_t NB, K, init_blocks, local_blocks;
+    int32_t vec_ok;  // table rows may be read with 16-byte loads
+};
+constexpr uint32_t kSelRowMax = 4096;  // row columns: out_stride <= 128 * 512 / 16
+constexpr int32_t kSelNBMax = 1024;    // pooled blocks: 4 * NB <= out_stride
+constexpr int32_t kSelKMax = 1024;
+constexpr uint32_t kSelOffRow = 0;
+constexpr uint32_t kSelOffHist = kSelOffRow + kSelRowMax * 2;
+constexpr uint32_t kSelOffIds = kSelOffHist + 2 * 256 * 4;
+constexpr uint32_t kSelOffMisc = kSelOffIds + kSelKMax * 4;
+constexpr uint32_t kSelBytes = kSelOffMisc + 32 * 4;
+constexpr uint32_t kDecOffSel = (kDecOffMisc + 64 + 127) & ~127u;
+constexpr uint32_t kDecSmemBytesSel = kDecOffSel + kSelBytes + 1024;
+static_assert(kDecSmemBytesSel <= 232448, "exceeds the 227 KB of shared memory a CTA may use");
+
 // N = 16 or 32 consecutive f32 columns of this thread's TMEM lane.
 template <int N>
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[N]);
@@ -852,6 +883,9 @@ struct DecItem {
     int32_t vis;      // visible compressed keys
     int32_t nkt;      // key tiles
     int64_t k_start;  // first compressed key of the token's sequence
+    int32_t seq;      // the token's sequence
+    int32_t lq;       // position of the token inside its sequence's queries
+    int32_t k_len;    // the sequence's compressed keys
     bool active;      // false: token outside every sequence or outside the token window
 };
 
@@ -868,6 +902,9 @@ __device__ __forceinline__ DecItem dec_decode(int64_t w, const Params &p, int32_
     it.vis = 0;
     it.nkt = 0;
     it.k_start = 0;
+    it.seq = 0;
+    it.lq = 0;
+    it.k_len = 0;
     if (p.n_seq <= 0 || it.t < p.t_begin || it.t >= p.t_end) return it;
     const int32_t t = (int32_t)it.t;
     if (t < __ldg(p.cu_q) || t >= __ldg(p.cu_q + p.n_seq)) return it;
@@ -880,6 +917,9 @@ __device__ __forceinline__ DecItem dec_decode(int64_t w, const Params &p, int32_
     const int32_t q_len = __ldg(p.cu_q + lo + 1) - qs;
     it.k_start = __ldg(p.cu_k + lo);
     const int32_t k_len = __ldg(p.cu_k + lo + 1) - (int32_t)it.k_start;
+    it.seq = lo;
+    it.lq = t - qs;
+    it.k_len = k_len;
     it.vis = visible(t - qs, q_len, k_len, p.causal);
     it.nkt = (it.vis + kBN - 1) / kBN;
     if (it.nkt > max_tiles) it.nkt = max_tiles;
@@ -957,10 +997,179 @@ __device__ __forceinline__ void dec_extra_scores8(const Params &p, const uint8_t
     }
 }
 
-template <int G>
+// Inclusive sum of v over the 256 epilogue threads; scratch: 8 words.  Ends with the
+// threads synchronised, so the scratch may be reused after the next barrier.
+__device__ __forceinline__ int32_t epi_scan(int32_t v, int32_t *scratch, int warp, int lane) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int32_t y = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += y;
+    }
+    if (lane == 31) scratch[warp] = v;
+    named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);
+    for (int w = 0; w < warp; ++w) v += scratch[w];
+    return v;
+}
+
+// Warp 0: find the bin of a 256-bin histogram (hist[b] = entries whose byte is b)
+// that holds the need-th largest entry, counting from bin 255 down.  Writes the bin to
+// out[0] and the count of entries in higher bins to out[1]; out[0] = -1 when the
+// histogram holds fewer than `need` entries; out[2] = the histogram's total.
+__device__ __forceinline__ void sel_find_bin(const int32_t *hist, int32_t need, int32_t *out, int lane) {
+    int32_t c[8], sum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        c[i] = hist[255 - 8 * lane - i];
+        sum += c[i];
+    }
+    int32_t incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    const int32_t total = __shfl_sync(0xffffffffu, incl, 31);
+    if (lane == 0) {
+        out[2] = total;
+        if (total < need) out[0] = -1;
+    }
+    int32_t run = incl - sum;
+    if (total >= need && run < need && incl >= need) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (run + c[i] >= need) {
+                out[0] = 255 - 8 * lane - i;
+                out[1] = run;
+                break;
+            }
+            run += c[i];
+        }
+    }
+}
+
+// Pooling, top-k and get_block_table of one decode item, by the 256 epilogue threads,
+// from the item's bf16 score row in shared memory (srow[j] = the value stage 1 writes at
+// column j; zeros past the tensor-memory tiles, as the written row has).
+//  - pooling: the window rule of max_pooling_1d_varlen (max_pooling_1d_varlen.py:69-116)
+//    with kernel 5, stride 4, padding 1 over the row read as flat stride out_stride (the
+//    caller's max_seqlen_q = 16 * out_stride), k_len = compressed keys + cache_lens[b],
+//    blocks j < init_blocks or with j <= off_bq <= j + local_blocks forced to +inf;
+//  - top-k: the rule of the top-k kernel: candidates are neither -inf nor NaN, ranked by
+//    (score desc, block asc), the first min(K, candidates) emitted in ascending block
+//    order, then -1;
+//  - get_block_table_ref_torch (get_table_torch.py:4-44) on the selected blocks.
+// Thread tid owns blocks 4*tid .. 4*tid+3, so a scan over threads orders blocks.
+__device__ __forceinline__ void dec_select(const Params &p, const DecSel &sel, const DecItem &it,
+                                           uint8_t *smem, int tid, int warp, int lane) {
+    const __nv_bfloat16 *srow = reinterpret_cast<const __nv_bfloat16 *>(smem + kSelOffRow);
+    int32_t *hist = reinterpret_cast<int32_t *>(smem + kSelOffHist);  // [2][256], zeroed by the caller
+    int32_t *sid = reinterpret_cast<int32_t *>(smem + kSelOffIds);
+    int32_t *misc = reinterpret_cast<int32_t *>(smem + kSelOffMisc);
+    const int32_t NB = sel.NB, K = sel.K;
+    int32_t k_len = 0, off_bq = 0;  // a token outside every sequence: k_len 0, local block 0
+    if (it.active) {
+        k_len = it.k_len + (sel.cache_lens ? __ldg(sel.cache_lens + it.seq) : 0);
+        off_bq = it.lq / 64;
+    }
+    const int64_t row = (int64_t)it.g * p.T + it.t;
+    uint32_t key[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const int32_t j = 4 * tid + e;
+        key[e] = 0;
+        if (j >= NB) continue;
+        uint16_t bits = 0xFF80u;  // -inf: no key under the window
+        const bool minf = j < sel.init_blocks || (off_bq >= j && off_bq <= j + sel.local_blocks);
+        if (minf) {
+            bits = 0x7F80u;
+        } else {
+            const int32_t ws = 4 * j - 1;
+            const int32_t lo = ws > 0 ? ws : 0;
+            const int32_t hi = ws + 5 < k_len ? ws + 5 : k_len;
+            if (hi > lo) {
+                float m = -INFINITY;
+                for (int32_t kp = lo; kp < hi; ++kp) m = fmaxf(m, __bfloat162float(srow[kp]));
+                bits = __bfloat16_as_ushort(__float2bfloat16_rn(m));
+            }
+        }
+        if (sel.pooled) sel.pooled[row * NB + j] = __ushort_as_bfloat16(bits);
+        const bool nan = (bits & 0x7F80u) == 0x7F80u && (bits & 0x7Fu) != 0;
+        if (bits != 0xFF80u && !nan) {
+            key[e] = (bits & 0x8000u) ? (~bits & 0xFFFFu) : (bits | 0x8000u);  // order-preserving
+            atomicAdd(hist + (key[e] >> 8), 1);
+        }
+    }
+    named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);
+    if (warp == 0) sel_find_bin(hist, K, misc + 8, lane);
+    named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);
+    const int32_t b1 = misc[8], n_cand = misc[10];
+    uint32_t thr = 0;  // selected: key > thr, and the first `need` keys == thr
+    int32_t need = 0;
+    if (b1 >= 0) {
+        const int32_t above = misc[9];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            if (key[e] != 0 && (int32_t)(key[e] >> 8) == b1) atomicAdd(hist + 256 + (key[e] & 255u), 1);
+        named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);
+        if (warp == 0) sel_find_bin(hist + 256, K - above, misc + 12, lane);
+        named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);
+        thr = ((uint32_t)b1 << 8) | (uint32_t)misc[12];
+        need = K - above - misc[13];
+    }
+    int32_t gt = 0, eq = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        gt += key[e] > thr;
+        eq += key[e] == thr && key[e] != 0;
+    }
+    const int32_t packed = (gt << 16) | eq;
+    const int32_t excl = epi_scan(packed, misc, warp, lane) - packed;
+    int32_t gt_before = excl >> 16, eq_before = excl & 0xFFFF;
+    int32_t *trow = sel.topk + row * K;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const int32_t j = 4 * tid + e;
+        int32_t pos = -1;
+        if (key[e] > thr) {
+            pos = gt_before + (eq_before < need ? eq_before : need);
+            ++gt_before;
+        } else if (key[e] == thr && key[e] != 0) {
+            if (eq_before < need) pos = gt_before + eq_before;
+            ++eq_before;
+        }
+        if (pos >= 0) {
+            sid[pos] = j;
+            trow[pos] = j;
+        }
+    }
+    const int32_t n_sel = n_cand < K ? n_cand : K;
+    for (int32_t i = n_sel + tid; i < K; i += kDecEpiWarps * 32) {
+        sid[i] = -1;
+        trow[i] = -1;
+    }
+    named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);
+    if (sel.slots) {
+        const int32_t t = (int32_t)it.t;
+        const int32_t bs = __ldg(sel.tok_bs + t);
+        const bool bs_ok = bs >= 0 && bs < sel.B;
+        const int32_t lim_pos = sel.pos_scalar ? __ldg(sel.tok_pos) : __ldg(sel.tok_pos + t);
+        const int32_t sl = sel.seqlen_scalar ? __ldg(sel.seqlen) : (bs_ok ? __ldg(sel.seqlen + bs) : 0);
+        const int32_t lim = bs_ok ? min(lim_pos, sl) : INT32_MIN;  // valid iff 0 <= pos < lim
+        const int32_t *brow = sel.table + (bs_ok ? (int64_t)bs * sel.bt_stride : 0);
+        const int32_t items = K * 16;  // int4 items of the row
+        const int32_t span = (items + kDecEpiWarps * 128 - 1) / (kDecEpiWarps * 128) * 128;
+        const int32_t eA = warp * span, eB = eA + span < items ? eA + span : items;
+        int4 *orow = reinterpret_cast<int4 *>(sel.slots + ((int64_t)it.t * p.Hk + it.g) * (int64_t)K * 64);
+        if (eA < items)
+            unum::gbt_emit_row<true>(sid, 1, K, brow, lim, sel.L, sel.head_group, (uint32_t)it.g,
+                                     sel.vec_ok != 0, orow, lane, eA, eB);
+    }
+}
+
+template <int G, bool kSel>
 __global__ void __launch_bounds__(kDecThreads, 1)
 stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                     const __grid_constant__ Params p) {
+                     const __grid_constant__ Params p, const __grid_constant__ DecSel sel) {
     constexpr uint32_t kQPanelD = G * 128;        // one 64-column panel of the token's G heads
     constexpr uint32_t kQBytesD = 2 * kQPanelD;
     constexpr uint32_t kIdesc = idesc_bf16_f32(128, G);
@@ -1107,6 +1316,18 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
             const DecItem it = dec_decode(w, p, (int32_t)kTmemCols / G);
             __nv_bfloat16 *orow = p.out + ((int64_t)it.g * p.T + it.t) * p.out_stride;
             int32_t zero_from = 0;  // first column of the row to zero-fill
+            __nv_bfloat16 *srow = reinterpret_cast<__nv_bfloat16 *>(sgen + kDecOffSel + kSelOffRow);
+            if constexpr (kSel) {
+                // the histograms, and the row's columns past its tensor-memory tiles that
+                // the pooling windows reach (4 * NB <= out_stride)
+                int32_t *hist = reinterpret_cast<int32_t *>(sgen + kDecOffSel + kSelOffHist);
+                for (int i = threadIdx.x; i < 512; i += kDecEpiWarps * 32) hist[i] = 0;
+                if (it.active) {
+                    const int32_t z0 = it.nkt * kBN, z1 = 4 * sel.NB;
+                    for (int32_t j = z0 + (int32_t)threadIdx.x; j < z1; j += kDecEpiWarps * 32)
+                        srow[j] = __float2bfloat16_rn(0.f);
+                }
+            }
             if (it.active && it.nkt > 0) {
                 const bool bad2 = !wait_bar(sy, tmem_full + 8 * s, (n / kDecSlots) & 1, 18);
                 if (named_bar_or(kDecEpiBarrier, kDecEpiWarps * 32, bad2)) break;
@@ -1186,7 +1407,11 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                             for (int i = 0; i < G; ++i) o += ex2(fmaf(vb[b][i], c, -m[i]));
                             o = fmaxf(o, 0.f);  // NaN scores give 0, as in the tile kernel
                         }
-                        if (j < p.out_stride) orow[j] = __float2bfloat16_rn(o);
+                        if (j < p.out_stride) {
+                            const __nv_bfloat16 ob = __float2bfloat16_rn(o);
+                            if (p.out) orow[j] = ob;
+                            if constexpr (kSel) srow[j] = ob;
+                        }
                     }
                 }
                 named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);  // every thread has read item_id[s]
@@ -1196,11 +1421,12 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                 named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);  // every thread has read item_id[s]
             }
             if (tid == 0) mbar_arrive(item_empty + 8 * s);
-            if (it.active && zero_from < p.out_stride) {
+            if (p.out && it.active && zero_from < p.out_stride) {
                 const int32_t n16 = (int32_t)((p.out_stride - zero_from) >> 3);
                 uint4 *dst = reinterpret_cast<uint4 *>(orow + zero_from);
                 for (int32_t e = tid; e < n16; e += kDecEpiWarps * 32) dst[e] = make_uint4(0u, 0u, 0u, 0u);
             }
+            if constexpr (kSel) dec_select(p, sel, it, sgen + kDecOffSel, tid, warp, lane);
         }
     }
 
@@ -1218,14 +1444,16 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
     }
 }
 
-template <int G>
-int launch_decode(const CUtensorMap &mq, const CUtensorMap &mk, const Params &p, cudaStream_t s) {
-    auto kern = stage1_decode_kernel<G>;
-    UNUM_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecSmemBytes));
+template <int G, bool kSel>
+int launch_decode(const CUtensorMap &mq, const CUtensorMap &mk, const Params &p, const DecSel &sel,
+                  cudaStream_t s) {
+    auto kern = stage1_decode_kernel<G, kSel>;
+    constexpr uint32_t smem = kSel ? kDecSmemBytesSel : kDecSmemBytes;
+    UNUM_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const int64_t items = p.T * p.Hk;
     const int64_t sms = unum::sm_count();
     const int grid = (int)(items < sms ? items : sms);
-    kern<<<grid, kDecThreads, kDecSmemBytes, s>>>(mq, mk, p);
+    kern<<<grid, kDecThreads, smem, s>>>(mq, mk, p, sel);
     return unum::check_launch("stage1_decode_kernel");
 }
 
@@ -1257,7 +1485,8 @@ int stage1_run(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, in
                const int32_t *cu_seqlens_q, const int32_t *cu_seqlens_k, int64_t n_seq,
                float softmax_scale, int causal, void *out, int64_t out_stride, void *workspace,
                size_t workspace_bytes, void *stream, void *pooled, int64_t NB, int64_t init_blocks,
-               int64_t local_blocks, int64_t t_begin = 0, int64_t t_end = INT64_MAX) {
+               int64_t local_blocks, int64_t t_begin = 0, int64_t t_end = INT64_MAX,
+               const DecSel *sel = nullptr) {
     UNUM_CHECK_ARG(T >= 0 && Tk >= 0 && Hq > 0 && Hk > 0 && n_seq >= 0 && out_stride >= 0,
                    "bad sizes");
     UNUM_CHECK_ARG(Hq % Hk == 0, "n_heads (%lld) must be a multiple of n_kv_heads (%lld)",
@@ -1273,7 +1502,7 @@ int stage1_run(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, in
         return UNUM_ERR_UNSUPPORTED;
     }
     UNUM_CHECK_ARG(out_stride % 128 == 0, "out_stride must be a multiple of 128");
-    UNUM_CHECK_ARG(q && (out || pooled) && cu_seqlens_q && cu_seqlens_k, "null pointer argument");
+    UNUM_CHECK_ARG(q && (out || pooled || sel) && cu_seqlens_q && cu_seqlens_k, "null pointer argument");
     UNUM_CHECK_ARG(unum::aligned16(out), "out must be 16-byte aligned");
     UNUM_CHECK_ARG(T < (int64_t)1 << 31 && Tk < (int64_t)1 << 31, "too many tokens");
     if (!workspace || workspace_bytes < unum_stage1_workspace_size(n_seq)) {
@@ -1312,7 +1541,7 @@ int stage1_run(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, in
     if (int rc = make_map(&mk, k, (uint64_t)D, (uint64_t)Hk, (uint64_t)Tk, (uint64_t)k_sh * 2,
                           (uint64_t)k_st * 2, 1, kBN))
         return rc;
-    if (use_decode_kernel(G, T, n_seq, out_stride, pooled)) {
+    if (sel || use_decode_kernel(G, T, n_seq, out_stride, pooled)) {
         CUtensorMap mqd;  // q with one token's G heads per box
         if (int rc = make_map(&mqd, q, (uint64_t)D, (uint64_t)Hq, (uint64_t)T, (uint64_t)q_sh * 2,
                               (uint64_t)q_st * 2, (uint32_t)G, 1))
@@ -1338,7 +1567,10 @@ int stage1_run(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, in
         p.k_st = k_st;
         p.k_sh = k_sh;
         p.force_expiry = force_expiry;
-        return G == 16 ? launch_decode<16>(mqd, mk, p, s) : launch_decode<32>(mqd, mk, p, s);
+        if (sel)
+            return G == 16 ? launch_decode<16, true>(mqd, mk, p, *sel, s) : launch_decode<32, true>(mqd, mk, p, *sel, s);
+        const DecSel none{};
+        return G == 16 ? launch_decode<16, false>(mqd, mk, p, none, s) : launch_decode<32, false>(mqd, mk, p, none, s);
     }
     CUtensorMap mo;  // out as a 2-D [Hk*T, out_stride] bf16 tensor, [64/G x 128] store boxes
     memset(&mo, 0, sizeof(mo));
@@ -1420,6 +1652,65 @@ extern "C" int unum_infllmv2_attn_stage1_pooled(
     return stage1_run(q, T, Hq, D, q_st, q_sh, k, Tk, Hk, k_st, k_sh, cu_seqlens_q, cu_seqlens_k,
                       n_seq, softmax_scale, causal, out, out_stride, workspace, workspace_bytes,
                       stream, pooled, NB, init_blocks, local_blocks);
+}
+
+extern "C" int unum_block_select_decode(
+    const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, int64_t q_sh, const void *k,
+    int64_t Tk, int64_t Hk, int64_t k_st, int64_t k_sh, const int32_t *cu_seqlens_q,
+    const int32_t *cu_seqlens_k, const int32_t *cache_lens, int64_t n_seq, float softmax_scale,
+    int causal, void *out, int64_t out_stride, void *pooled, int64_t NB, int64_t init_blocks,
+    int64_t local_blocks, int32_t *topk_idx, int64_t K, int32_t *slots, const int32_t *block_table,
+    int64_t B, int64_t L, int64_t bt_stride, const int32_t *token_to_bs, const int32_t *token_pos_in_bs,
+    int pos_is_scalar, const int32_t *seqlen_q, int seqlen_is_scalar, int32_t head_group,
+    void *workspace, size_t workspace_bytes, void *stream) {
+    unum::clear_error();
+    UNUM_CHECK_ARG(Hk > 0 && Hq > 0 && Hq % Hk == 0, "n_heads must be a multiple of n_kv_heads");
+    const int64_t G = Hq / Hk;
+    if (!(G == 16 || G == 32) || D != kD || n_seq <= 0 || Tk <= 0 ||
+        out_stride > (int64_t)kBN * ((int64_t)kTmemCols / G)) {
+        unum::set_error("fused decode selection needs G in {16, 32}, head_dim 128, at least one "
+                        "sequence and compressed key, and out_stride <= %lld",
+                        (long long)(kBN * (kTmemCols / (G > 0 ? G : 1))));
+        return UNUM_ERR_UNSUPPORTED;
+    }
+    if (NB <= 0 || NB > kSelNBMax || 4 * NB > out_stride || K <= 0 || K > kSelKMax) {
+        unum::set_error("fused decode selection needs 0 < NB, 4 * NB <= out_stride (the pooling "
+                        "windows inside the row) and 0 < K <= %d", (int)kSelKMax);
+        return UNUM_ERR_UNSUPPORTED;
+    }
+    UNUM_CHECK_ARG(init_blocks >= -(1 << 30) && init_blocks < (1 << 30) && local_blocks >= -(1 << 30) &&
+                       local_blocks < (1 << 30),
+                   "pooling parameters out of range");
+    UNUM_CHECK_ARG(topk_idx != nullptr, "topk_idx output required");
+    if (slots) {
+        UNUM_CHECK_ARG(block_table && token_to_bs && token_pos_in_bs && seqlen_q && B > 0 && L > 0 &&
+                           L <= (int64_t)INT32_MAX && B <= (int64_t)INT32_MAX && bt_stride >= L,
+                       "slots need a non-empty block table and the token maps");
+        UNUM_CHECK_ARG(unum::aligned16(slots), "slots must be 16-byte aligned");
+    }
+    DecSel sel{};
+    sel.cache_lens = cache_lens;
+    sel.pooled = (__nv_bfloat16 *)pooled;
+    sel.topk = topk_idx;
+    sel.slots = slots;
+    sel.table = block_table;
+    sel.tok_bs = token_to_bs;
+    sel.tok_pos = token_pos_in_bs;
+    sel.seqlen = seqlen_q;
+    sel.bt_stride = bt_stride;
+    sel.B = (int32_t)B;
+    sel.L = (int32_t)L;
+    sel.pos_scalar = pos_is_scalar ? 1 : 0;
+    sel.seqlen_scalar = seqlen_is_scalar ? 1 : 0;
+    sel.head_group = (uint32_t)head_group;
+    sel.NB = (int32_t)NB;
+    sel.K = (int32_t)K;
+    sel.init_blocks = (int32_t)init_blocks;
+    sel.local_blocks = (int32_t)local_blocks;
+    sel.vec_ok = unum::aligned16(block_table) && (bt_stride % 4 == 0);
+    return stage1_run(q, T, Hq, D, q_st, q_sh, k, Tk, Hk, k_st, k_sh, cu_seqlens_q, cu_seqlens_k,
+                      n_seq, softmax_scale, causal, out, out_stride, workspace, workspace_bytes,
+                      stream, nullptr, 0, 0, 0, 0, INT64_MAX, &sel);
 }
 
 extern "C" int unum_stage1_status(const void *workspace, void *stream, int32_t *status_out) {
