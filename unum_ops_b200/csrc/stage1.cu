@@ -673,6 +673,10 @@ stage1_prologue(const int32_t *__restrict__ cu_q, int32_t n_seq, int32_t QT, int
                 __nv_bfloat16 *pooled, int32_t NB, int32_t init_blocks, int32_t local_blocks) {
     __shared__ int32_t warp_sums[32];
     __shared__ int32_t carry_s;
+    // a decode kernel launched after this one with programmatic stream serialization
+    // may start its set-up now; it waits (griddepcontrol.wait) for this grid to finish
+    // before it touches the workspace
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) {
         ws[0] = 0;
@@ -1047,6 +1051,37 @@ __device__ __forceinline__ void sel_find_bin(const int32_t *hist, int32_t need, 
     }
 }
 
+// Per-token values the selection needs from global memory, loaded when the epilogue
+// takes the item so that their latency hides behind its three passes.
+struct SelPre {
+    int32_t k_len;   // the pooling's key count: compressed keys + cache_lens[b]
+    int32_t off_bq;  // the token's local block
+    int32_t lim;     // get_block_table: positions valid iff 0 <= pos < lim
+    int64_t brow;    // offset of the token's block-table row
+};
+
+__device__ __forceinline__ SelPre dec_sel_pre(const DecSel &sel, const DecItem &it) {
+    SelPre r;
+    r.k_len = 0;  // a token outside every sequence: k_len 0, local block 0
+    r.off_bq = 0;
+    if (it.active) {
+        r.k_len = it.k_len + (sel.cache_lens ? __ldg(sel.cache_lens + it.seq) : 0);
+        r.off_bq = it.lq / 64;
+    }
+    r.lim = INT32_MIN;
+    r.brow = 0;
+    if (sel.slots) {
+        const int32_t t = (int32_t)it.t;
+        const int32_t bs = __ldg(sel.tok_bs + t);
+        const bool bs_ok = bs >= 0 && bs < sel.B;
+        const int32_t lim_pos = sel.pos_scalar ? __ldg(sel.tok_pos) : __ldg(sel.tok_pos + t);
+        const int32_t sl = sel.seqlen_scalar ? __ldg(sel.seqlen) : (bs_ok ? __ldg(sel.seqlen + bs) : 0);
+        r.lim = bs_ok ? min(lim_pos, sl) : INT32_MIN;
+        r.brow = bs_ok ? (int64_t)bs * sel.bt_stride : 0;
+    }
+    return r;
+}
+
 // Pooling, top-k and get_block_table of one decode item, by the 256 epilogue threads,
 // from the item's bf16 score row in shared memory (srow[j] = the value stage 1 writes at
 // column j; zeros past the tensor-memory tiles, as the written row has).
@@ -1060,17 +1095,13 @@ __device__ __forceinline__ void sel_find_bin(const int32_t *hist, int32_t need, 
 //  - get_block_table_ref_torch (get_table_torch.py:4-44) on the selected blocks.
 // Thread tid owns blocks 4*tid .. 4*tid+3, so a scan over threads orders blocks.
 __device__ __forceinline__ void dec_select(const Params &p, const DecSel &sel, const DecItem &it,
-                                           uint8_t *smem, int tid, int warp, int lane) {
+                                           const SelPre &pre, uint8_t *smem, int tid, int warp, int lane) {
     const __nv_bfloat16 *srow = reinterpret_cast<const __nv_bfloat16 *>(smem + kSelOffRow);
     int32_t *hist = reinterpret_cast<int32_t *>(smem + kSelOffHist);  // [2][256], zeroed by the caller
     int32_t *sid = reinterpret_cast<int32_t *>(smem + kSelOffIds);
     int32_t *misc = reinterpret_cast<int32_t *>(smem + kSelOffMisc);
     const int32_t NB = sel.NB, K = sel.K;
-    int32_t k_len = 0, off_bq = 0;  // a token outside every sequence: k_len 0, local block 0
-    if (it.active) {
-        k_len = it.k_len + (sel.cache_lens ? __ldg(sel.cache_lens + it.seq) : 0);
-        off_bq = it.lq / 64;
-    }
+    const int32_t k_len = pre.k_len, off_bq = pre.off_bq;
     const int64_t row = (int64_t)it.g * p.T + it.t;
     uint32_t key[4];
 #pragma unroll
@@ -1149,13 +1180,8 @@ __device__ __forceinline__ void dec_select(const Params &p, const DecSel &sel, c
     }
     named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);
     if (sel.slots) {
-        const int32_t t = (int32_t)it.t;
-        const int32_t bs = __ldg(sel.tok_bs + t);
-        const bool bs_ok = bs >= 0 && bs < sel.B;
-        const int32_t lim_pos = sel.pos_scalar ? __ldg(sel.tok_pos) : __ldg(sel.tok_pos + t);
-        const int32_t sl = sel.seqlen_scalar ? __ldg(sel.seqlen) : (bs_ok ? __ldg(sel.seqlen + bs) : 0);
-        const int32_t lim = bs_ok ? min(lim_pos, sl) : INT32_MIN;  // valid iff 0 <= pos < lim
-        const int32_t *brow = sel.table + (bs_ok ? (int64_t)bs * sel.bt_stride : 0);
+        const int32_t lim = pre.lim;
+        const int32_t *brow = sel.table + pre.brow;
         const int32_t items = K * 16;  // int4 items of the row
         const int32_t span = (items + kDecEpiWarps * 128 - 1) / (kDecEpiWarps * 128) * 128;
         const int32_t eA = warp * span, eB = eA + span < items ? eA + span : items;
@@ -1205,11 +1231,7 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
         }
         for (int i = 0; i < kDecSlots; ++i) mbar_init(tmem_full + 8 * i, 1);
         for (uint32_t i = 0; i < kTs; ++i) mbar_init(slot_empty + 8 * i, 4);  // a tile's 4 reader warps
-        *abort_flag = 0;
-        if (p.force_expiry) {
-            *abort_flag = 1;
-            atomicCAS(p.ws, 0, 30);
-        }
+        *abort_flag = p.force_expiry ? 1 : 0;  // status 30 is set after the prologue
         fence_barrier_init();
     }
     if (warp == kDecProducerWarp && lane == 0) {
@@ -1224,6 +1246,10 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // set-up above overlaps the prologue's tail; the workspace (status, work counter) and
+    // the rows the prologue zeroes are touched only after it has finished
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (threadIdx.x == 0 && p.force_expiry) atomicCAS(p.ws, 0, 30);
     const int64_t n_items = p.T * p.Hk;
     int32_t *counter = p.ws + 1;
 
@@ -1317,7 +1343,9 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
             __nv_bfloat16 *orow = p.out + ((int64_t)it.g * p.T + it.t) * p.out_stride;
             int32_t zero_from = 0;  // first column of the row to zero-fill
             __nv_bfloat16 *srow = reinterpret_cast<__nv_bfloat16 *>(sgen + kDecOffSel + kSelOffRow);
+            SelPre pre{};
             if constexpr (kSel) {
+                pre = dec_sel_pre(sel, it);
                 // the histograms, and the row's columns past its tensor-memory tiles that
                 // the pooling windows reach (4 * NB <= out_stride)
                 int32_t *hist = reinterpret_cast<int32_t *>(sgen + kDecOffSel + kSelOffHist);
@@ -1426,7 +1454,7 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                 uint4 *dst = reinterpret_cast<uint4 *>(orow + zero_from);
                 for (int32_t e = tid; e < n16; e += kDecEpiWarps * 32) dst[e] = make_uint4(0u, 0u, 0u, 0u);
             }
-            if constexpr (kSel) dec_select(p, sel, it, sgen + kDecOffSel, tid, warp, lane);
+            if constexpr (kSel) dec_select(p, sel, it, pre, sgen + kDecOffSel, tid, warp, lane);
         }
     }
 
@@ -1453,7 +1481,19 @@ int launch_decode(const CUtensorMap &mq, const CUtensorMap &mk, const Params &p,
     const int64_t items = p.T * p.Hk;
     const int64_t sms = unum::sm_count();
     const int grid = (int)(items < sms ? items : sms);
-    kern<<<grid, kDecThreads, smem, s>>>(mq, mk, p, sel);
+    // launched with programmatic stream serialization: its CTAs start while the
+    // prologue (the previous launch on the stream) runs, and wait for it in-kernel
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kDecThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    UNUM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, mq, mk, p, sel));
     return unum::check_launch("stage1_decode_kernel");
 }
 
