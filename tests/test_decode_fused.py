@@ -96,10 +96,18 @@ def _assert_same(got, ref, scores=True):
         assert torch.equal(a, r), f"{name} differs at {int((a != r).sum())} positions"
 
 
+@pytest.fixture(params=["pairs", "single"])
+def cta_mode(request, monkeypatch):
+    """Both forms of the decode kernel: items shared by CTA pairs (a cluster of two) and
+    one CTA per item (UNUM_DECODE_PAIRS forces the choice, read at every launch)."""
+    monkeypatch.setenv("UNUM_DECODE_PAIRS", "1" if request.param == "pairs" else "0")
+    return request.param
+
+
 @pytest.mark.parametrize("hq", [32, 64])
 @pytest.mark.parametrize("with_cache", [True, False])
 @pytest.mark.parametrize("K", [64, 16])
-def test_fused_decode_equals_chain(hq, with_cache, K, dev):
+def test_fused_decode_equals_chain(hq, with_cache, K, dev, cta_mode):
     b = _batch(100 + hq + K, dev, hq=hq)
     W = _round128(b["max_k"])
     ctx_max = min(16384 if hq == 32 else 8192, 16 * W)  # 4 * NB <= W
@@ -118,7 +126,7 @@ def test_fused_decode_without_scores(dev):
     _assert_same(got, ref, scores=False)
 
 
-def test_fused_decode_edge_rows(dev):
+def test_fused_decode_edge_rows(dev, cta_mode):
     """Tokens outside every sequence, empty sequences, two-token sequences, sequences
     with no compressed key, fewer candidates than K (-1 padding), K above NB."""
     q_per = np.array([1, 0, 2, 1, 1, 0, 2, 1, 1, 1, 2, 1])
@@ -132,7 +140,7 @@ def test_fused_decode_edge_rows(dev):
             _assert_same(got, ref)
 
 
-def test_fused_decode_ties_and_scalar_maps(dev):
+def test_fused_decode_ties_and_scalar_maps(dev, cta_mode):
     """Equal keys give equal scores inside a row (ties ranked by block index), and a
     scalar token_pos_in_bs / seqlen_q broadcast like the reference's numel()==1 case."""
     b = _batch(13, dev, same_keys=True)
@@ -144,7 +152,7 @@ def test_fused_decode_ties_and_scalar_maps(dev):
     _assert_same(got, ref)
 
 
-def test_fused_decode_vs_oracle(dev, oracle_lib):
+def test_fused_decode_vs_oracle(dev, oracle_lib, cta_mode):
     """Downstream of the GPU's own stage-1 scores, the fused pooled blocks, ids and slots
     equal the C oracle's pooling, top-k and get_block_table; the scores themselves are
     within the fp32 oracle's tolerance."""
@@ -177,3 +185,25 @@ def test_block_select_routes_decode_batches(dev):
                        b["seqlen"], max_context_len=16 * W, cache_lens=b["cache"])
     ref = _chain(b, 16 * W, b["cache"], 1, 2, 64)
     _assert_same(got, ref)
+
+
+def test_pairs_match_single_cta_within_tolerance(dev, oracle_lib, monkeypatch):
+    """The CTA-pair kernel sums each head's statistics in two halves, so its scores may
+    differ from the one-CTA kernel's in the last bits only: both within the oracle's
+    tolerance, and close to each other.  Covers items with one tile (the peer holds none)
+    and rows longer than one CTA's tensor memory holds (out_stride below the keys)."""
+    from unum_ops_b200.infllm_v2 import infllmv2_attn_stage1
+
+    b = _batch(23, dev, B=20, ctx_lo=20, ctx_hi=60000)
+    for mk in (b["max_k"], 1024):
+        outs = {}
+        for mode in ("1", "0"):
+            monkeypatch.setenv("UNUM_DECODE_PAIRS", mode)
+            outs[mode] = infllmv2_attn_stage1(b["q"], b["k"], None, b["cu_q"], b["cu_k"],
+                                              max_seqlen_k=mk, causal=True).float()
+        torch.cuda.synchronize()
+        torch.testing.assert_close(outs["1"], outs["0"], atol=1e-3, rtol=1e-2)
+        orc = oracle_lib.stage1(b["q"].float().cpu().numpy(), b["k"].float().cpu().numpy(),
+                                b["cu_q"].cpu().numpy(), b["cu_k"].cpu().numpy(), True,
+                                out_stride=outs["1"].shape[-1])
+        np.testing.assert_allclose(outs["1"].cpu().numpy(), orc, atol=1e-3, rtol=1e-2)

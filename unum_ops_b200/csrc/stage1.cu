@@ -172,12 +172,20 @@ struct Sync {
 };
 
 // Bounded wait: false once this CTA has given up (then callers stop issuing work).
+// kCluster: the barrier is arrived on by another CTA of the cluster, whose writes before
+// its arrive must be visible here (acquire at cluster scope).
+template <bool kCluster = false>
+__device__ __forceinline__ bool try_wait_scoped(uint32_t bar, uint32_t parity) {
+    return kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
+}
+
+template <bool kCluster = false>
 __device__ __forceinline__ bool wait_bar(const Sync &s, uint32_t bar, uint32_t parity, int code) {
     if (*s.abort) return false;
-    if (mbar_try_wait(bar, parity)) return true;
+    if (try_wait_scoped<kCluster>(bar, parity)) return true;
     const uint64_t t_start = globaltimer_ns();
     for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (try_wait_scoped<kCluster>(bar, parity)) return true;
         if ((i & 63) == 0) {
             if (*s.abort) return false;
             if (globaltimer_ns() - t_start > kWaitNs) {
@@ -818,7 +826,7 @@ constexpr int kDecEpiBarrier = 1;
 constexpr uint32_t kDecQSlot = 2 * 32 * 128;                 // two 64-column panels of up to 32 heads
 constexpr uint32_t kDecOffK = kDecSlots * kDecQSlot;          // 32 KB
 constexpr uint32_t kDecOffRed = kDecOffK + kDecStages * kKStage;
-constexpr uint32_t kDecOffBar = kDecOffRed + 2 * kDecEpiWarps * 32 * 4;
+constexpr uint32_t kDecOffBar = kDecOffRed + 2 * (kDecEpiWarps + 1) * 32 * 4;
 // barriers: item_full, item_empty, q_full, tmem_full (per item slot), k_full, k_empty (per
 // stage), and one per TMEM tile slot (free again)
 constexpr int kDecTmemSlotsMax = 32;  // 512 columns / 16 heads
@@ -854,8 +862,16 @@ constexpr uint32_t kSelOffHist = kSelOffRow + kSelRowMax * 2;
 constexpr uint32_t kSelOffIds = kSelOffHist + 2 * 256 * 4;
 constexpr uint32_t kSelOffMisc = kSelOffIds + kSelKMax * 4;
 constexpr uint32_t kSelBytes = kSelOffMisc + 32 * 4;
-constexpr uint32_t kDecOffSel = (kDecOffMisc + 64 + 127) & ~127u;
+// CTA pairs (a cluster of two sharing each item): the peer's item mailbox, the
+// exchanged per-head statistics and the barriers of the exchange
+constexpr uint32_t kDecOffPair = (kDecOffMisc + 64 + 15) & ~15u;
+constexpr uint32_t kPairInbox = 0;                        // int64 [kDecSlots]
+constexpr uint32_t kPairX = kPairInbox + 8 * kDecSlots;   // float [2][32]: peer's max, sum
+constexpr uint32_t kPairBars = kPairX + 2 * 32 * 4;       // item_in[slots], peer_empty[slots], x_full[2], row_full
+constexpr uint32_t kPairBytes = kPairBars + (2 * kDecSlots + 3) * 8;
+constexpr uint32_t kDecOffSel = (kDecOffPair + kPairBytes + 127) & ~127u;
 constexpr uint32_t kDecSmemBytesSel = kDecOffSel + kSelBytes + 1024;
+constexpr uint32_t kDecSmemBytesPair = kDecOffSel + 1024;
 static_assert(kDecSmemBytesSel <= 232448, "exceeds the 227 KB of shared memory a CTA may use");
 
 // N = 16 or 32 consecutive f32 columns of this thread's TMEM lane.
@@ -931,30 +947,42 @@ __device__ __forceinline__ DecItem dec_decode(int64_t w, const Params &p, int32_
     return it;
 }
 
-// Warp-wide max (or sum) of each of N per-thread values, then across the 4
-// epilogue warps through shared memory; every epilogue thread gets the results.
+// Max (or sum) of each of N per-thread values (N = 16 or 32) over the 256 epilogue
+// threads; every thread gets the N results.  In a warp, a reduce-scatter: at each step a
+// lane keeps half of its values and receives its partner's copy of that half, so after
+// log2(N) steps lane L holds value L % N reduced over N lanes (N - 1 shuffles instead of
+// 5N); then across the 8 warps through shared memory `red` ([9][32] floats: the warps'
+// partials, then the results).
 template <int N, bool kMax>
 __device__ __forceinline__ void dec_reduce(float (&v)[N], float *red, int warp, int lane) {
+    static_assert(N == 16 || N == 32, "16 or 32 values");
 #pragma unroll
-    for (int i = 0; i < N; ++i) {
+    for (int h = N / 2; h >= 1; h >>= 1) {
+        const bool upper = (lane & h) != 0;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float y = __shfl_xor_sync(0xffffffffu, v[i], o);
-            v[i] = kMax ? fmaxf(v[i], y) : v[i] + y;
+        for (int i = 0; i < h; ++i) {
+            const float send = upper ? v[i] : v[i + h];
+            const float keep = upper ? v[i + h] : v[i];
+            const float got = __shfl_xor_sync(0xffffffffu, send, h);
+            v[i] = kMax ? fmaxf(keep, got) : keep + got;
         }
     }
-    if (lane == 0) {
+    float x = v[0];  // value lane % N, over the N lanes that share lane / N
+    if (N < 32) {
+        const float y = __shfl_xor_sync(0xffffffffu, x, 16);
+        x = kMax ? fmaxf(x, y) : x + y;
+    }
+    if (lane < N) red[warp * 32 + lane] = x;
+    named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);
+    if (warp == 0 && lane < N) {
+        float a = red[lane];
 #pragma unroll
-        for (int i = 0; i < N; ++i) red[warp * 32 + i] = v[i];
+        for (int w2 = 1; w2 < kDecEpiWarps; ++w2) a = kMax ? fmaxf(a, red[w2 * 32 + lane]) : a + red[w2 * 32 + lane];
+        red[kDecEpiWarps * 32 + lane] = a;
     }
     named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);
 #pragma unroll
-    for (int i = 0; i < N; ++i) {
-        float a = red[i];
-#pragma unroll
-        for (int w2 = 1; w2 < kDecEpiWarps; ++w2) a = kMax ? fmaxf(a, red[w2 * 32 + i]) : a + red[w2 * 32 + i];
-        v[i] = a;
-    }
+    for (int i = 0; i < N; ++i) v[i] = red[kDecEpiWarps * 32 + i];
 }
 
 // Named barrier over n threads that also ORs a predicate across them, so a
@@ -1015,11 +1043,15 @@ __device__ __forceinline__ int32_t epi_scan(int32_t v, int32_t *scratch, int war
     return v;
 }
 
-// Warp 0: find the bin of a 256-bin histogram (hist[b] = entries whose byte is b)
-// that holds the need-th largest entry, counting from bin 255 down.  Writes the bin to
-// out[0] and the count of entries in higher bins to out[1]; out[0] = -1 when the
-// histogram holds fewer than `need` entries; out[2] = the histogram's total.
-__device__ __forceinline__ void sel_find_bin(const int32_t *hist, int32_t need, int32_t *out, int lane) {
+// The bin of a 256-bin histogram (hist[b] = entries whose byte is b) that holds the
+// need-th largest entry, counting from bin 255 down, and the count of entries in higher
+// bins; bin -1 when the histogram holds fewer than `need` entries.  Computed by every
+// warp that calls it (the same result in every lane), so no barrier is needed to share it.
+struct BinPick {
+    int32_t bin, above, total;
+};
+
+__device__ __forceinline__ BinPick sel_pick_bin(const int32_t *hist, int32_t need, int lane) {
     int32_t c[8], sum = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -1032,23 +1064,32 @@ __device__ __forceinline__ void sel_find_bin(const int32_t *hist, int32_t need, 
         const int32_t y = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += y;
     }
-    const int32_t total = __shfl_sync(0xffffffffu, incl, 31);
-    if (lane == 0) {
-        out[2] = total;
-        if (total < need) out[0] = -1;
-    }
-    int32_t run = incl - sum;
-    if (total >= need && run < need && incl >= need) {
+    BinPick r;
+    r.total = __shfl_sync(0xffffffffu, incl, 31);
+    r.bin = -1;
+    r.above = 0;
+    if (r.total < need) return r;
+    const int32_t excl = incl - sum;
+    const unsigned hit = __ballot_sync(0xffffffffu, excl < need && incl >= need);
+    const int src = __ffs(hit) - 1;
+    int32_t bin = -1, above = 0, run = excl;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            if (run + c[i] >= need) {
-                out[0] = 255 - 8 * lane - i;
-                out[1] = run;
-                break;
-            }
-            run += c[i];
+    for (int i = 0; i < 8; ++i) {
+        if (bin < 0 && run + c[i] >= need) {
+            bin = 255 - 8 * lane - i;
+            above = run;
         }
+        run += c[i];
     }
+    r.bin = __shfl_sync(0xffffffffu, bin, src);
+    r.above = __shfl_sync(0xffffffffu, above, src);
+    return r;
+}
+
+// Add one to hist[bin] for every lane with bin >= 0, one atomic per distinct bin of the warp.
+__device__ __forceinline__ void hist_add_warp(int32_t *hist, int32_t bin, int lane) {
+    const unsigned peers = __match_any_sync(0xffffffffu, bin);
+    if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(hist + bin, __popc(peers));
 }
 
 // Per-token values the selection needs from global memory, loaded when the epilogue
@@ -1103,49 +1144,62 @@ __device__ __forceinline__ void dec_select(const Params &p, const DecSel &sel, c
     const int32_t NB = sel.NB, K = sel.K;
     const int32_t k_len = pre.k_len, off_bq = pre.off_bq;
     const int64_t row = (int64_t)it.g * p.T + it.t;
+    // the 17 row values the 4 windows of this thread read: columns 16*tid - 1 .. 16*tid + 15,
+    // masked to -inf outside [0, k_len) (the reference's window bounds)
+    float v[17];
+    {
+        const uint4 *src = reinterpret_cast<const uint4 *>(srow) + 2 * tid;
+        const uint4 a = src[0], b = src[1];
+        const __nv_bfloat16 *pa = reinterpret_cast<const __nv_bfloat16 *>(&a);
+        const __nv_bfloat16 *pb = reinterpret_cast<const __nv_bfloat16 *>(&b);
+        const int32_t c0 = 16 * tid;
+        v[0] = (c0 >= 1 && c0 - 1 < k_len) ? __bfloat162float(srow[c0 - 1]) : -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            v[1 + i] = c0 + i < k_len ? __bfloat162float(pa[i]) : -INFINITY;
+            v[9 + i] = c0 + 8 + i < k_len ? __bfloat162float(pb[i]) : -INFINITY;
+        }
+    }
     uint32_t key[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
         const int32_t j = 4 * tid + e;
         key[e] = 0;
-        if (j >= NB) continue;
-        uint16_t bits = 0xFF80u;  // -inf: no key under the window
-        const bool minf = j < sel.init_blocks || (off_bq >= j && off_bq <= j + sel.local_blocks);
-        if (minf) {
-            bits = 0x7F80u;
-        } else {
-            const int32_t ws = 4 * j - 1;
-            const int32_t lo = ws > 0 ? ws : 0;
-            const int32_t hi = ws + 5 < k_len ? ws + 5 : k_len;
-            if (hi > lo) {
-                float m = -INFINITY;
-                for (int32_t kp = lo; kp < hi; ++kp) m = fmaxf(m, __bfloat162float(srow[kp]));
+        int32_t bin = -1;
+        if (j < NB) {
+            uint16_t bits;
+            const bool minf = j < sel.init_blocks || (off_bq >= j && off_bq <= j + sel.local_blocks);
+            if (minf) {
+                bits = 0x7F80u;
+            } else {  // window columns 4j-1 .. 4j+3 = v[4e .. 4e+4]; all masked: -inf
+                const float m = fmaxf(fmaxf(fmaxf(v[4 * e], v[4 * e + 1]), fmaxf(v[4 * e + 2], v[4 * e + 3])),
+                                      v[4 * e + 4]);
                 bits = __bfloat16_as_ushort(__float2bfloat16_rn(m));
             }
+            if (sel.pooled) sel.pooled[row * NB + j] = __ushort_as_bfloat16(bits);
+            const bool nan = (bits & 0x7F80u) == 0x7F80u && (bits & 0x7Fu) != 0;
+            if (bits != 0xFF80u && !nan) {
+                key[e] = (bits & 0x8000u) ? (~bits & 0xFFFFu) : (bits | 0x8000u);  // order-preserving
+                bin = (int32_t)(key[e] >> 8);
+            }
         }
-        if (sel.pooled) sel.pooled[row * NB + j] = __ushort_as_bfloat16(bits);
-        const bool nan = (bits & 0x7F80u) == 0x7F80u && (bits & 0x7Fu) != 0;
-        if (bits != 0xFF80u && !nan) {
-            key[e] = (bits & 0x8000u) ? (~bits & 0xFFFFu) : (bits | 0x8000u);  // order-preserving
-            atomicAdd(hist + (key[e] >> 8), 1);
-        }
+        hist_add_warp(hist, bin, lane);
     }
     named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);
-    if (warp == 0) sel_find_bin(hist, K, misc + 8, lane);
-    named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);
-    const int32_t b1 = misc[8], n_cand = misc[10];
+    const BinPick p1 = sel_pick_bin(hist, K, lane);
+    const int32_t n_cand = p1.total;
     uint32_t thr = 0;  // selected: key > thr, and the first `need` keys == thr
     int32_t need = 0;
-    if (b1 >= 0) {
-        const int32_t above = misc[9];
+    if (p1.bin >= 0) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-            if (key[e] != 0 && (int32_t)(key[e] >> 8) == b1) atomicAdd(hist + 256 + (key[e] & 255u), 1);
+        for (int e = 0; e < 4; ++e) {
+            const bool in = key[e] != 0 && (int32_t)(key[e] >> 8) == p1.bin;
+            hist_add_warp(hist + 256, in ? (int32_t)(key[e] & 255u) : -1, lane);
+        }
         named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);
-        if (warp == 0) sel_find_bin(hist + 256, K - above, misc + 12, lane);
-        named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);
-        thr = ((uint32_t)b1 << 8) | (uint32_t)misc[12];
-        need = K - above - misc[13];
+        const BinPick p2 = sel_pick_bin(hist + 256, K - p1.above, lane);
+        thr = ((uint32_t)p1.bin << 8) | (uint32_t)p2.bin;
+        need = K - p1.above - p2.above;
     }
     int32_t gt = 0, eq = 0;
 #pragma unroll
@@ -1192,7 +1246,14 @@ __device__ __forceinline__ void dec_select(const Params &p, const DecSel &sel, c
     }
 }
 
-template <int G, bool kSel>
+// kC = 2: the kernel runs as clusters of two CTAs, each pair working on one item at a
+// time: the leader (rank 0) takes items and posts them to its peer, each CTA streams the
+// key tiles of its own parity (tile kt goes to rank kt % 2), the per-head max and sum are
+// exchanged through distributed shared memory, and the peer's bf16 outputs are written
+// into the leader's row buffer, where the leader runs the fused selection.  Halves the
+// time of an item: for batches with fewer items than SMs, where the longest item bounds
+// the kernel (one SM streams keys at well below its share of HBM bandwidth).
+template <int G, bool kSel, int kC>
 __global__ void __launch_bounds__(kDecThreads, 1)
 stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ Params p, const __grid_constant__ DecSel sel) {
@@ -1203,7 +1264,7 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t sbase = (raw + 1023u) & ~1023u;
     uint8_t *sgen = smem_raw + (sbase - raw);
-    float *red = reinterpret_cast<float *>(sgen + kDecOffRed);  // [2][4 warps][32]
+    float *red = reinterpret_cast<float *>(sgen + kDecOffRed);  // [2][9][32]: max and sum reductions
     const uint32_t bar0 = sbase + kDecOffBar;
     const uint32_t item_full = bar0, item_empty = bar0 + 8 * kDecSlots, q_full = bar0 + 16 * kDecSlots;
     const uint32_t k_full = bar0 + 24 * kDecSlots, k_empty = k_full + 8 * kDecStages;
@@ -1219,7 +1280,25 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
     sy.abort = abort_flag;
     sy.status = p.ws;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr bool kPair = kC == 2;
+    const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+    const uint32_t pbase = sbase + kDecOffPair;
+    volatile int64_t *inbox = reinterpret_cast<volatile int64_t *>(sgen + kDecOffPair + kPairInbox);
+    volatile float *xbuf = reinterpret_cast<volatile float *>(sgen + kDecOffPair + kPairX);
+    const uint32_t item_in = pbase + kPairBars, peer_empty = item_in + 8 * kDecSlots;
+    const uint32_t x_full = peer_empty + 8 * kDecSlots, row_full = x_full + 16;
+    // the tile capacity of an item: tensor memory of every CTA of the pair
+    constexpr int32_t kMaxTiles = (int32_t)(kTmemCols / G) * kC;
     if (threadIdx.x == 0) {
+        if constexpr (kPair) {
+            for (int i = 0; i < kDecSlots; ++i) {
+                mbar_init(item_in + 8 * i, 1);     // the leader's post (peer)
+                mbar_init(peer_empty + 8 * i, 1);  // the peer took the post (leader)
+            }
+            mbar_init(x_full, 1);                  // the other CTA's max
+            mbar_init(x_full + 8, 1);              // the other CTA's sum
+            mbar_init(row_full, kDecEpiWarps * 32);  // the peer's outputs are in srow (leader)
+        }
         for (int i = 0; i < kDecSlots; ++i) {
             mbar_init(item_full + 8 * i, 1);
             mbar_init(item_empty + 8 * i, 2);  // the MMA warp's commit + the epilogue
@@ -1244,6 +1323,7 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (kPair) cluster_sync();  // both CTAs' barriers exist before any remote arrive
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     // set-up above overlaps the prologue's tail; the workspace (status, work counter) and
@@ -1256,14 +1336,29 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
     if (warp == kDecProducerWarp) {
         if (lane == 0) {
             uint32_t kc = 0;
+            const int64_t n_groups = gridDim.x / kC;  // CTAs (pairs) taking items
             for (uint32_t n = 0;; ++n) {
-                const uint32_t s = n % kDecSlots;
-                if (!wait_bar(sy, item_empty + 8 * s, ((n / kDecSlots) & 1) ^ 1, 11)) break;
-                int64_t w = atomicAdd(counter, 1);
-                if (w >= n_items) w = -1;
-                const DecItem it = w >= 0 ? dec_decode(w, p, (int32_t)kTmemCols / G) : DecItem{};
+                const uint32_t s = n % kDecSlots, eph = ((n / kDecSlots) & 1) ^ 1;
+                if (!wait_bar(sy, item_empty + 8 * s, eph, 11)) break;
+                int64_t w;
+                if (rank == 0) {
+                    // first item static (no counter round trip on the critical path), then dynamic
+                    w = n == 0 ? (int64_t)(blockIdx.x / kC) : atomicAdd(counter, 1) + n_groups;
+                    if (w >= n_items) w = -1;
+                    if constexpr (kPair) {  // post it to the peer once it has taken the last post
+                        if (!wait_bar<true>(sy, peer_empty + 8 * s, eph, 19)) break;
+                        st_cluster_s64(mapa_shared(pbase + kPairInbox + 8 * s, 1), w);
+                        mbar_arrive_remote(mapa_shared(item_in + 8 * s, 1));
+                    }
+                } else {
+                    if (!wait_bar<true>(sy, item_in + 8 * s, (n / kDecSlots) & 1, 19)) break;
+                    w = inbox[s];
+                    mbar_arrive_remote(mapa_shared(peer_empty + 8 * s, 0));
+                }
+                const DecItem it = w >= 0 ? dec_decode(w, p, kMaxTiles) : DecItem{};
+                const int32_t nl = (it.nkt - (int32_t)rank + kC - 1) / kC;  // this CTA's tiles
                 item_id[s] = w;
-                if (w >= 0 && it.nkt > 0) {
+                if (w >= 0 && nl > 0) {
                     mbar_arrive_expect_tx(q_full + 8 * s, kQBytesD);
                     const uint32_t qd = sbase + s * kDecQSlot;
                     tma_load_3d(qd, &tmQ, 0, it.g * G, (int32_t)it.t, q_full + 8 * s);
@@ -1273,10 +1368,11 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                 }
                 mbar_arrive(item_full + 8 * s);
                 if (w < 0) break;
-                for (int32_t kt = 0; kt < it.nkt; ++kt, ++kc) {
+                for (int32_t i = 0; i < nl; ++i, ++kc) {
                     const uint32_t st = kc % kDecStages, ph = (kc / kDecStages) & 1;
                     if (!wait_bar(sy, k_empty + 8 * st, ph ^ 1, 12)) break;
                     const uint32_t dst = sbase + kDecOffK + st * kKStage;
+                    const int32_t kt = kC * i + (int32_t)rank;  // the item's tile
                     const int32_t krow = (int32_t)(it.k_start + (int64_t)kt * kBN);
                     mbar_arrive_expect_tx(k_full + 8 * st, kKStage);
                     tma_load_3d(dst, &tmK, 0, it.g, krow, k_full + 8 * st);
@@ -1293,8 +1389,9 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                 if (!wait_bar(sy, item_full + 8 * s, sph, 13)) break;
                 const int64_t w = item_id[s];
                 if (w < 0) break;
-                const DecItem it = dec_decode(w, p, (int32_t)kTmemCols / G);
-                if (it.nkt == 0) {
+                const DecItem it = dec_decode(w, p, kMaxTiles);
+                const int32_t nl = (it.nkt - (int32_t)rank + kC - 1) / kC;
+                if (nl <= 0) {
                     mbar_arrive(tmem_full + 8 * s);  // one phase per use of the slot
                     mbar_arrive(item_empty + 8 * s);
                     continue;
@@ -1302,7 +1399,7 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                 bool ok = wait_bar(sy, q_full + 8 * s, sph, 15);
                 tc_fence_after();
                 const uint32_t qb = sbase + s * kDecQSlot;
-                for (int32_t kt = 0; ok && kt < it.nkt; ++kt, ++kc, ++tc) {
+                for (int32_t kt = 0; ok && kt < nl; ++kt, ++kc, ++tc) {
                     const uint32_t st = kc % kDecStages, slot = tc % kTs;
                     ok = wait_bar(sy, slot_empty + 8 * slot, ((tc / kTs) & 1) ^ 1, 14);
                     ok = ok && wait_bar(sy, k_full + 8 * st, (kc / kDecStages) & 1, 16);
@@ -1333,18 +1430,21 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
         const float c = p.c;
         uint32_t tbase = 0;  // TMEM tiles consumed
+        uint32_t xn = 0;     // items whose statistics were exchanged with the peer
         for (uint32_t n = 0;; ++n) {
             const uint32_t s = n % kDecSlots;
             const bool bad = !wait_bar(sy, item_full + 8 * s, (n / kDecSlots) & 1, 17);
             if (named_bar_or(kDecEpiBarrier, kDecEpiWarps * 32, bad)) break;  // gave up: all leave
             const int64_t w = item_id[s];
             if (w < 0) break;
-            const DecItem it = dec_decode(w, p, (int32_t)kTmemCols / G);
+            const DecItem it = dec_decode(w, p, kMaxTiles);
+            const int32_t nl = (it.nkt - (int32_t)rank + kC - 1) / kC;  // this CTA's tiles
             __nv_bfloat16 *orow = p.out + ((int64_t)it.g * p.T + it.t) * p.out_stride;
             int32_t zero_from = 0;  // first column of the row to zero-fill
             __nv_bfloat16 *srow = reinterpret_cast<__nv_bfloat16 *>(sgen + kDecOffSel + kSelOffRow);
+            const uint32_t srow_leader = kPair ? mapa_shared(sbase + kDecOffSel + kSelOffRow, 0) : 0u;
             SelPre pre{};
-            if constexpr (kSel) {
+            if (kSel && rank == 0) {
                 pre = dec_sel_pre(sel, it);
                 // the histograms, and the row's columns past its tensor-memory tiles that
                 // the pooling windows reach (4 * NB <= out_stride)
@@ -1357,26 +1457,29 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                 }
             }
             if (it.active && it.nkt > 0) {
-                const bool bad2 = !wait_bar(sy, tmem_full + 8 * s, (n / kDecSlots) & 1, 18);
-                if (named_bar_or(kDecEpiBarrier, kDecEpiWarps * 32, bad2)) break;
-                tc_fence_after();
-                // TMEM reads in batches of kTB tiles (64 columns) per wait
+                // TMEM reads in batches of kTB tiles (64 columns); local tile i of this CTA is
+                // the item's tile kC*i + rank, key column col(i)
                 constexpr int kTB = 64 / G;
                 float vb[kTB][G], m[G], l[G];
+                auto col = [&](int32_t i) { return (kC * i + (int32_t)rank) * kBN + key; };
                 auto load_batch = [&](int32_t kt0) {
 #pragma unroll
                     for (int b = 0; b < kTB; ++b)
-                        if (kt0 + b < it.nkt)
+                        if (kt0 + b < nl)
                             tmem_ld_cols<G>(tmem + lane_base + ((tbase + kt0 + b) % kTs) * G, vb[b]);
                     tmem_wait_ld();
                 };
+                const uint32_t xph = xn & 1;
+                const bool bad2 = !wait_bar(sy, tmem_full + 8 * s, (n / kDecSlots) & 1, 18);
+                if (named_bar_or(kDecEpiBarrier, kDecEpiWarps * 32, bad2)) break;
+                tc_fence_after();
 #pragma unroll
                 for (int i = 0; i < G; ++i) m[i] = -INFINITY;
-                for (int32_t kt0 = par * kTB; kt0 < it.nkt; kt0 += 2 * kTB) {
+                for (int32_t kt0 = par * kTB; kt0 < nl; kt0 += 2 * kTB) {
                     load_batch(kt0);
 #pragma unroll
                     for (int b = 0; b < kTB; ++b) {
-                        if ((kt0 + b) * kBN + key < it.vis) {
+                        if (col(kt0 + b) < it.vis) {
 #pragma unroll
                             for (int i = 0; i < G; ++i) m[i] = fmaxf(m[i], vb[b][i]);
                         }
@@ -1385,7 +1488,7 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                 // keys past the tensor-memory tiles (an out_stride below the sequence's key
                 // count): into the statistics only, on CUDA cores
                 const uint8_t *qtile = sgen + s * kDecQSlot;
-                for (int32_t j = it.nkt * kBN + tid; j < it.vis; j += kDecEpiWarps * 32) {
+                for (int32_t j = it.nkt * kBN + tid; rank == 0 && j < it.vis; j += kDecEpiWarps * 32) {
 #pragma unroll
                     for (int h0 = 0; h0 < G; h0 += 8) {
                         float sc[8];
@@ -1395,19 +1498,31 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                     }
                 }
                 dec_reduce<G, true>(m, red, warp, lane);
+                if constexpr (kPair) {  // the pair's max: this CTA's and the peer's
+                    if (tid == 0) {
+                        const uint32_t rx = mapa_shared(pbase + kPairX, rank ^ 1u);
+#pragma unroll
+                        for (int i = 0; i < G; ++i) st_cluster_f32(rx + 4 * i, m[i]);
+                        mbar_arrive_remote(mapa_shared(x_full, rank ^ 1u));
+                    }
+                    const bool bx = !wait_bar<true>(sy, x_full, xph, 20);
+                    if (named_bar_or(kDecEpiBarrier, kDecEpiWarps * 32, bx)) break;
+#pragma unroll
+                    for (int i = 0; i < G; ++i) m[i] = fmaxf(m[i], xbuf[i]);
+                }
 #pragma unroll
                 for (int i = 0; i < G; ++i) l[i] = 0.f;
-                for (int32_t kt0 = par * kTB; kt0 < it.nkt; kt0 += 2 * kTB) {
+                for (int32_t kt0 = par * kTB; kt0 < nl; kt0 += 2 * kTB) {
                     load_batch(kt0);
 #pragma unroll
                     for (int b = 0; b < kTB; ++b) {
-                        if ((kt0 + b) * kBN + key < it.vis) {
+                        if (col(kt0 + b) < it.vis) {
 #pragma unroll
                             for (int i = 0; i < G; ++i) l[i] += ex2((vb[b][i] - m[i]) * c);
                         }
                     }
                 }
-                for (int32_t j = it.nkt * kBN + tid; j < it.vis; j += kDecEpiWarps * 32) {
+                for (int32_t j = it.nkt * kBN + tid; rank == 0 && j < it.vis; j += kDecEpiWarps * 32) {
 #pragma unroll
                     for (int h0 = 0; h0 < G; h0 += 8) {
                         float sc[8];
@@ -1416,19 +1531,31 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                         for (int i = 0; i < 8; ++i) l[h0 + i] += ex2((sc[i] - m[h0 + i]) * c);
                     }
                 }
-                dec_reduce<G, false>(l, red + kDecEpiWarps * 32, warp, lane);
+                dec_reduce<G, false>(l, red + (kDecEpiWarps + 1) * 32, warp, lane);
+                if constexpr (kPair) {  // the pair's sum (both halves taken against the pair's max)
+                    if (tid == 0) {
+                        const uint32_t rx = mapa_shared(pbase + kPairX + 128, rank ^ 1u);
+#pragma unroll
+                        for (int i = 0; i < G; ++i) st_cluster_f32(rx + 4 * i, l[i]);
+                        mbar_arrive_remote(mapa_shared(x_full + 8, rank ^ 1u));
+                    }
+                    const bool bx = !wait_bar<true>(sy, x_full + 8, xph, 21);
+                    if (named_bar_or(kDecEpiBarrier, kDecEpiWarps * 32, bx)) break;
+#pragma unroll
+                    for (int i = 0; i < G; ++i) l[i] += xbuf[32 + i];
+                }
 #pragma unroll
                 for (int i = 0; i < G; ++i) m[i] = fmaf(m[i], c, log2f(l[i]));  // b = m*c + log2(l)
-                for (int32_t kt0 = par * kTB; kt0 < it.nkt; kt0 += 2 * kTB) {
+                for (int32_t kt0 = par * kTB; kt0 < nl; kt0 += 2 * kTB) {
                     load_batch(kt0);
                     // this warp's last read of these tiles: their slots may take new tiles
                     tc_fence_before();
                     __syncwarp();
-                    if (lane < kTB && kt0 + lane < it.nkt) mbar_arrive(slot_empty + 8 * ((tbase + kt0 + lane) % kTs));
+                    if (lane < kTB && kt0 + lane < nl) mbar_arrive(slot_empty + 8 * ((tbase + kt0 + lane) % kTs));
 #pragma unroll
                     for (int b = 0; b < kTB; ++b) {
-                        const int32_t j = (kt0 + b) * kBN + key;
-                        if (kt0 + b >= it.nkt) break;
+                        const int32_t j = col(kt0 + b);
+                        if (kt0 + b >= nl) break;
                         float o = 0.f;
                         if (j < it.vis) {
 #pragma unroll
@@ -1438,17 +1565,28 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                         if (j < p.out_stride) {
                             const __nv_bfloat16 ob = __float2bfloat16_rn(o);
                             if (p.out) orow[j] = ob;
-                            if constexpr (kSel) srow[j] = ob;
+                            if constexpr (kSel) {
+                                if (rank == 0) srow[j] = ob;
+                                else st_cluster_u16(srow_leader + 2 * j, __bfloat16_as_ushort(ob));
+                            }
                         }
                     }
                 }
+                if (kPair && kSel && rank != 0) mbar_arrive_remote(mapa_shared(row_full, 0));
                 named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);  // every thread has read item_id[s]
-                tbase += (uint32_t)it.nkt;
+                tbase += (uint32_t)nl;
                 zero_from = it.nkt * kBN;
             } else {
                 named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);  // every thread has read item_id[s]
             }
             if (tid == 0) mbar_arrive(item_empty + 8 * s);
+            const bool exchanged = it.active && it.nkt > 0;
+            if (kPair && exchanged) ++xn;
+            if (rank != 0) continue;  // the leader writes the row's tail and runs the selection
+            if (kPair && kSel && exchanged) {  // the peer's columns have landed in srow
+                const bool br = !wait_bar<true>(sy, row_full, (xn - 1) & 1, 22);
+                if (named_bar_or(kDecEpiBarrier, kDecEpiWarps * 32, br)) break;
+            }
             if (p.out && it.active && zero_from < p.out_stride) {
                 const int32_t n16 = (int32_t)((p.out_stride - zero_from) >> 3);
                 uint4 *dst = reinterpret_cast<uint4 *>(orow + zero_from);
@@ -1470,17 +1608,21 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
+    if constexpr (kPair) {
+        __syncthreads();
+        cluster_sync();  // neither CTA leaves while the other may still write into it
+    }
 }
 
-template <int G, bool kSel>
+template <int G, bool kSel, int kC>
 int launch_decode(const CUtensorMap &mq, const CUtensorMap &mk, const Params &p, const DecSel &sel,
                   cudaStream_t s) {
-    auto kern = stage1_decode_kernel<G, kSel>;
-    constexpr uint32_t smem = kSel ? kDecSmemBytesSel : kDecSmemBytes;
+    auto kern = stage1_decode_kernel<G, kSel, kC>;
+    constexpr uint32_t smem = kSel ? kDecSmemBytesSel : (kC == 2 ? kDecSmemBytesPair : kDecSmemBytes);
     UNUM_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const int64_t items = p.T * p.Hk;
-    const int64_t sms = unum::sm_count();
-    const int grid = (int)(items < sms ? items : sms);
+    const int64_t groups = unum::sm_count() / kC;  // CTAs (pairs) taking items
+    const int grid = (int)(items < groups ? items : groups) * kC;
     // launched with programmatic stream serialization: its CTAs start while the
     // prologue (the previous launch on the stream) runs, and wait for it in-kernel
     cudaLaunchConfig_t cfg = {};
@@ -1488,11 +1630,15 @@ int launch_decode(const CUtensorMap &mq, const CUtensorMap &mk, const Params &p,
     cfg.blockDim = dim3(kDecThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = kC;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     UNUM_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, mq, mk, p, sel));
     return unum::check_launch("stage1_decode_kernel");
 }
@@ -1518,6 +1664,17 @@ bool use_decode_kernel(int64_t G, int64_t T, int64_t n_seq, int64_t out_stride, 
     if (env && strcmp(env, "tile") == 0) return false;
     if (env && strcmp(env, "decode") == 0) return true;
     return T <= 4 * n_seq;
+}
+
+// Decode items shared by CTA pairs when every pair gets at most one item (items <= SMs/2):
+// then the longest item bounds the kernel, and a pair streams it at about twice the
+// rate of one SM.  With more items, pairs measured slower (two rounds of items where
+// single CTAs need one).  UNUM_DECODE_PAIRS=0 or =1 forces the choice, for testing.
+bool use_pairs(int64_t items) {
+    const char *env = getenv("UNUM_DECODE_PAIRS");
+    if (env && env[0] == '0') return false;
+    if (env && env[0] == '1') return true;
+    return 2 * items <= unum::sm_count();
 }
 
 int stage1_run(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, int64_t q_sh,
@@ -1607,10 +1764,20 @@ int stage1_run(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, in
         p.k_st = k_st;
         p.k_sh = k_sh;
         p.force_expiry = force_expiry;
-        if (sel)
-            return G == 16 ? launch_decode<16, true>(mqd, mk, p, *sel, s) : launch_decode<32, true>(mqd, mk, p, *sel, s);
+        const bool pair = use_pairs(T * Hk);
+        if (sel) {
+            if (pair)
+                return G == 16 ? launch_decode<16, true, 2>(mqd, mk, p, *sel, s)
+                               : launch_decode<32, true, 2>(mqd, mk, p, *sel, s);
+            return G == 16 ? launch_decode<16, true, 1>(mqd, mk, p, *sel, s)
+                           : launch_decode<32, true, 1>(mqd, mk, p, *sel, s);
+        }
         const DecSel none{};
-        return G == 16 ? launch_decode<16, false>(mqd, mk, p, none, s) : launch_decode<32, false>(mqd, mk, p, none, s);
+        if (pair)
+            return G == 16 ? launch_decode<16, false, 2>(mqd, mk, p, none, s)
+                           : launch_decode<32, false, 2>(mqd, mk, p, none, s);
+        return G == 16 ? launch_decode<16, false, 1>(mqd, mk, p, none, s)
+                       : launch_decode<32, false, 1>(mqd, mk, p, none, s);
     }
     CUtensorMap mo;  // out as a 2-D [Hk*T, out_stride] bf16 tensor, [64/G x 128] store boxes
     memset(&mo, 0, sizeof(mo));
