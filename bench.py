@@ -293,10 +293,15 @@ def run_ours(args):
     def gather_idx(local_idx, shards):
         exchange_shards(local_idx, full_idx, shards, rank, wire=wire_idx)
 
+    # the exchange runs on a side stream once top-k is done, overlapping get_block_table
+    # (an HBM-bound kernel, while the exchange is NVLink traffic); the step ends when both do
+    xstream = torch.cuda.Stream(dev) if world > 1 else None
+    topk_done = torch.cuda.Event()
+
     def step(ev=None):
         """One block-selection pass over this rank's shard: stage 1 with the pooling
         fused in (token window [ta, tb_) of kv heads g0..g0+nh-1), top-k, get_block_table;
-        with several ranks, the top-k ids are then gathered on every rank."""
+        with several ranks, the top-k ids are gathered on every rank meanwhile."""
         if ev is not None:
             ev[0].record(stream)
         unum_ops_b200._lib.check(L.unum_infllmv2_attn_stage1_window(
@@ -316,12 +321,21 @@ def run_ours(args):
                     stream.cuda_stream))
         if ev is not None:
             ev[2].record(stream)
+        if world > 1:
+            topk_done.record(stream)
+            xstream.wait_event(topk_done)
+            with torch.cuda.stream(xstream):
+                if ev is not None:
+                    ev[5].record(xstream)
+                gather_idx(idx, ranges)
+                if ev is not None:
+                    ev[6].record(xstream)
         get_block_table_shard(idx, d["table"], d["tb"][ta:tb_], d["pos"][ta:tb_], d["seqlen"],
                               head_offset=g0, out=slots)
         if ev is not None:
             ev[3].record(stream)
         if world > 1:
-            gather_idx(idx, ranges)
+            stream.wait_stream(xstream)
         if ev is not None:
             ev[4].record(stream)
 
@@ -337,7 +351,7 @@ def run_ours(args):
     if stage1_status(dev) != 0:
         raise RuntimeError("stage-1 kernel reported a timeout")
 
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(args.steps)]
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     barrier()
@@ -350,12 +364,25 @@ def run_ours(args):
     wall1 = time.time()
     clk.stop()
     total_ms = t_start.elapsed_time(t_end)
-    per = {"stage1": [], "topk": [], "get_block_table": [], "gather": []}
+    if world > 1:
+        # the overlapped exchange delivered the ids: this rank's own shard is in place, and
+        # every rank holds the same gathered tensor
+        torch.cuda.synchronize(dev)
+        assert torch.equal(full_idx[g0:g0 + nh, ta:tb_], idx), "own top-k shard missing after the exchange"
+        w = torch.arange(1, full_idx.numel() + 1, device=dev, dtype=torch.int64).view(full_idx.shape)
+        sums = torch.stack([(full_idx.to(torch.int64) * w).sum()] * 2)
+        lo, hi = sums.clone(), sums.clone()
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+        assert int(lo[0]) == int(hi[0]), "ranks hold different gathered top-k ids"
+    per = {"stage1": [], "topk": [], "get_block_table": [], "gather": [], "tail": []}
     for e in evs:
         per["stage1"].append(e[0].elapsed_time(e[1]))
         per["topk"].append(e[1].elapsed_time(e[2]))
         per["get_block_table"].append(e[2].elapsed_time(e[3]))
-        per["gather"].append(e[3].elapsed_time(e[4]))
+        if world > 1:
+            per["gather"].append(e[5].elapsed_time(e[6]))
+            per["tail"].append(e[2].elapsed_time(e[4]))
     ms_step = total_ms / args.steps
     if world > 1:
         t = torch.tensor([ms_step], device=dev)
@@ -479,7 +506,7 @@ def run_ours(args):
     if rank == 0:
         clocks = clk.summary(wall0, wall1)
         hbm, tf_burst, tf_sus, src = load_peaks()
-        mean = {k: statistics.mean(v) for k, v in per.items()}
+        mean = {k: statistics.mean(v) for k, v in per.items() if v}
         flops = stage1_flops(ta, tb_) * nh / HK
         ab = algorithmic_bytes(nrows, nh)
         traffic = load_traffic()
@@ -495,7 +522,9 @@ def run_ours(args):
         if world > 1:
             kernels["topk_idx_gather"] = {"ms": mean["gather"], "bytes": full_idx.numel() * 2,
                                           "how": "NCCL send/recv of each rank's exact shard, int16 "
-                                                 "on the wire, widened to int32 once"}
+                                                 "on the wire, widened to int32 once; on a side "
+                                                 "stream, overlapping get_block_table",
+                                          "after_topk_ms": mean["tail"]}
         cpu = None
         if args.cpu_sample > 0 and world == 1:
             hf = {k: v.numpy() for k, v in host.items() if k not in ("q", "k")}
@@ -598,6 +627,10 @@ def measure_decode(args, world, rank, dev, steps=None, warmup=None):
     else:
         plan = [list(range(B_all))] * world
     mine = np.array(plan[rank], np.int64)
+    # longest sequences first: the decode kernel takes (token, kv head) items in order, so
+    # the longest start first and the shorter ones fill in behind them (the order a decode
+    # scheduler can give its batch; the work is the same)
+    mine = mine[np.argsort(-k_lens_all[mine], kind="stable")]
     B = len(mine)
     starts = np.concatenate([[0], np.cumsum(k_lens_all)])
     k_rows = np.concatenate([np.arange(starts[i], starts[i + 1]) for i in mine])
