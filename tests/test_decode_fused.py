@@ -96,11 +96,16 @@ def _assert_same(got, ref, scores=True):
         assert torch.equal(a, r), f"{name} differs at {int((a != r).sum())} positions"
 
 
-@pytest.fixture(params=["pairs", "single"])
+@pytest.fixture(params=["pairs", "hybrid", "single"])
 def cta_mode(request, monkeypatch):
-    """Both forms of the decode kernel: items shared by CTA pairs (a cluster of two) and
-    one CTA per item (UNUM_DECODE_PAIRS forces the choice, read at every launch)."""
-    monkeypatch.setenv("UNUM_DECODE_PAIRS", "1" if request.param == "pairs" else "0")
+    """Every form of the decode kernel: items shared by CTA pairs (a cluster of two), pairs
+    that share the first 5 items and give later ones to one CTA each, and one CTA per item
+    (UNUM_DECODE_PAIRS / UNUM_DECODE_JOINT_ITEMS force the choice, read at every launch)."""
+    monkeypatch.setenv("UNUM_DECODE_PAIRS", "0" if request.param == "single" else "1")
+    if request.param == "hybrid":
+        monkeypatch.setenv("UNUM_DECODE_JOINT_ITEMS", "5")
+    else:
+        monkeypatch.delenv("UNUM_DECODE_JOINT_ITEMS", raising=False)
     return request.param
 
 
@@ -197,13 +202,16 @@ def test_pairs_match_single_cta_within_tolerance(dev, oracle_lib, monkeypatch):
     b = _batch(23, dev, B=20, ctx_lo=20, ctx_hi=60000)
     for mk in (b["max_k"], 1024):
         outs = {}
-        for mode in ("1", "0"):
+        for mode, jt in (("1", "999"), ("1", "8"), ("0", "0")):
             monkeypatch.setenv("UNUM_DECODE_PAIRS", mode)
-            outs[mode] = infllmv2_attn_stage1(b["q"], b["k"], None, b["cu_q"], b["cu_k"],
-                                              max_seqlen_k=mk, causal=True).float()
+            monkeypatch.setenv("UNUM_DECODE_JOINT_ITEMS", jt)
+            outs[mode + jt] = infllmv2_attn_stage1(b["q"], b["k"], None, b["cu_q"], b["cu_k"],
+                                                   max_seqlen_k=mk, causal=True).float()
         torch.cuda.synchronize()
-        torch.testing.assert_close(outs["1"], outs["0"], atol=1e-3, rtol=1e-2)
+        torch.testing.assert_close(outs["1999"], outs["00"], atol=1e-3, rtol=1e-2)
+        torch.testing.assert_close(outs["18"], outs["00"], atol=1e-3, rtol=1e-2)
         orc = oracle_lib.stage1(b["q"].float().cpu().numpy(), b["k"].float().cpu().numpy(),
                                 b["cu_q"].cpu().numpy(), b["cu_k"].cpu().numpy(), True,
-                                out_stride=outs["1"].shape[-1])
-        np.testing.assert_allclose(outs["1"].cpu().numpy(), orc, atol=1e-3, rtol=1e-2)
+                                out_stride=outs["1999"].shape[-1])
+        for key in ("1999", "18"):
+            np.testing.assert_allclose(outs[key].cpu().numpy(), orc, atol=1e-3, rtol=1e-2)

@@ -114,6 +114,9 @@ struct Params {
     // nonzero: every bounded wait reports expiry at once (status 30) before any
     // TMA or UMMA work is issued, so the drain path can be tested without a fault
     int32_t force_expiry;
+    // decode kernel in CTA pairs: items 0 .. joint_items-1 are shared by a pair, later ones
+    // go to one CTA of a pair alone
+    int64_t joint_items;
 };
 
 struct Item {
@@ -1092,6 +1095,28 @@ __device__ __forceinline__ void hist_add_warp(int32_t *hist, int32_t bin, int la
     if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(hist + bin, __popc(peers));
 }
 
+// A decode item as the pair's leader posts it: its id, plus kSoloBit when one CTA takes
+// it alone rather than the pair sharing it; -1 ends the stream.  A CTA's share of the
+// item: tiles cr, cr + cc, cr + 2cc, ... (joint: cr = rank, cc = 2; alone: 0, 1).
+constexpr int64_t kSoloBit = (int64_t)1 << 40;
+
+struct Role {
+    int64_t w;     // item id, or -1
+    bool joint;    // shared by the pair
+    int32_t cr, cc, max_tiles;
+};
+
+template <int kC>
+__device__ __forceinline__ Role role_of(int64_t v, uint32_t rank, int32_t tmem_tiles) {
+    Role r;
+    r.joint = kC == 2 && v >= 0 && (v & kSoloBit) == 0;
+    r.w = v >= 0 ? (v & (kSoloBit - 1)) : -1;
+    r.cr = r.joint ? (int32_t)rank : 0;
+    r.cc = r.joint ? 2 : 1;
+    r.max_tiles = tmem_tiles * r.cc;
+    return r;
+}
+
 // Per-token values the selection needs from global memory, loaded when the epilogue
 // takes the item so that their latency hides behind its three passes.
 struct SelPre {
@@ -1287,8 +1312,6 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
     volatile float *xbuf = reinterpret_cast<volatile float *>(sgen + kDecOffPair + kPairX);
     const uint32_t item_in = pbase + kPairBars, peer_empty = item_in + 8 * kDecSlots;
     const uint32_t x_full = peer_empty + 8 * kDecSlots, row_full = x_full + 16;
-    // the tile capacity of an item: tensor memory of every CTA of the pair
-    constexpr int32_t kMaxTiles = (int32_t)(kTmemCols / G) * kC;
     if (threadIdx.x == 0) {
         if constexpr (kPair) {
             for (int i = 0; i < kDecSlots; ++i) {
@@ -1337,27 +1360,40 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
         if (lane == 0) {
             uint32_t kc = 0;
             const int64_t n_groups = gridDim.x / kC;  // CTAs (pairs) taking items
+            bool peer_done = false;                     // the peer was sent the end of the stream
             for (uint32_t n = 0;; ++n) {
                 const uint32_t s = n % kDecSlots, eph = ((n / kDecSlots) & 1) ^ 1;
                 if (!wait_bar(sy, item_empty + 8 * s, eph, 11)) break;
-                int64_t w;
+                int64_t v;  // this CTA's item as posted (id, solo bit)
                 if (rank == 0) {
                     // first item static (no counter round trip on the critical path), then dynamic
-                    w = n == 0 ? (int64_t)(blockIdx.x / kC) : atomicAdd(counter, 1) + n_groups;
-                    if (w >= n_items) w = -1;
-                    if constexpr (kPair) {  // post it to the peer once it has taken the last post
-                        if (!wait_bar<true>(sy, peer_empty + 8 * s, eph, 19)) break;
-                        st_cluster_s64(mapa_shared(pbase + kPairInbox + 8 * s, 1), w);
-                        mbar_arrive_remote(mapa_shared(item_in + 8 * s, 1));
+                    int64_t w1 = n == 0 ? (int64_t)(blockIdx.x / kC) : atomicAdd(counter, 1) + n_groups;
+                    if (w1 >= n_items) w1 = -1;
+                    v = w1;
+                    if constexpr (kPair) {
+                        int64_t vp = w1;  // the peer's
+                        if (w1 >= 0 && w1 >= p.joint_items) {  // one item each
+                            v = w1 | kSoloBit;
+                            const int64_t w2 = atomicAdd(counter, 1) + n_groups;
+                            vp = w2 < n_items ? (w2 | kSoloBit) : -1;
+                        }
+                        if (!peer_done) {  // post it once the peer has taken the last post
+                            if (!wait_bar<true>(sy, peer_empty + 8 * s, eph, 19)) break;
+                            st_cluster_s64(mapa_shared(pbase + kPairInbox + 8 * s, 1), vp);
+                            mbar_arrive_remote(mapa_shared(item_in + 8 * s, 1));
+                            peer_done = vp < 0;  // the counter is spent: nothing more for either
+                        }
                     }
                 } else {
                     if (!wait_bar<true>(sy, item_in + 8 * s, (n / kDecSlots) & 1, 19)) break;
-                    w = inbox[s];
+                    v = inbox[s];
                     mbar_arrive_remote(mapa_shared(peer_empty + 8 * s, 0));
                 }
-                const DecItem it = w >= 0 ? dec_decode(w, p, kMaxTiles) : DecItem{};
-                const int32_t nl = (it.nkt - (int32_t)rank + kC - 1) / kC;  // this CTA's tiles
-                item_id[s] = w;
+                const Role ro = role_of<kC>(v, rank, kTs);
+                const int64_t w = ro.w;
+                const DecItem it = w >= 0 ? dec_decode(w, p, ro.max_tiles) : DecItem{};
+                const int32_t nl = (it.nkt - ro.cr + ro.cc - 1) / ro.cc;  // this CTA's tiles
+                item_id[s] = v;
                 if (w >= 0 && nl > 0) {
                     mbar_arrive_expect_tx(q_full + 8 * s, kQBytesD);
                     const uint32_t qd = sbase + s * kDecQSlot;
@@ -1372,7 +1408,7 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                     const uint32_t st = kc % kDecStages, ph = (kc / kDecStages) & 1;
                     if (!wait_bar(sy, k_empty + 8 * st, ph ^ 1, 12)) break;
                     const uint32_t dst = sbase + kDecOffK + st * kKStage;
-                    const int32_t kt = kC * i + (int32_t)rank;  // the item's tile
+                    const int32_t kt = ro.cc * i + ro.cr;  // the item's tile
                     const int32_t krow = (int32_t)(it.k_start + (int64_t)kt * kBN);
                     mbar_arrive_expect_tx(k_full + 8 * st, kKStage);
                     tma_load_3d(dst, &tmK, 0, it.g, krow, k_full + 8 * st);
@@ -1387,10 +1423,10 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
             for (uint32_t n = 0;; ++n) {
                 const uint32_t s = n % kDecSlots, sph = (n / kDecSlots) & 1;
                 if (!wait_bar(sy, item_full + 8 * s, sph, 13)) break;
-                const int64_t w = item_id[s];
-                if (w < 0) break;
-                const DecItem it = dec_decode(w, p, kMaxTiles);
-                const int32_t nl = (it.nkt - (int32_t)rank + kC - 1) / kC;
+                const Role ro = role_of<kC>(item_id[s], rank, kTs);
+                if (ro.w < 0) break;
+                const DecItem it = dec_decode(ro.w, p, ro.max_tiles);
+                const int32_t nl = (it.nkt - ro.cr + ro.cc - 1) / ro.cc;
                 if (nl <= 0) {
                     mbar_arrive(tmem_full + 8 * s);  // one phase per use of the slot
                     mbar_arrive(item_empty + 8 * s);
@@ -1435,16 +1471,19 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
             const uint32_t s = n % kDecSlots;
             const bool bad = !wait_bar(sy, item_full + 8 * s, (n / kDecSlots) & 1, 17);
             if (named_bar_or(kDecEpiBarrier, kDecEpiWarps * 32, bad)) break;  // gave up: all leave
-            const int64_t w = item_id[s];
-            if (w < 0) break;
-            const DecItem it = dec_decode(w, p, kMaxTiles);
-            const int32_t nl = (it.nkt - (int32_t)rank + kC - 1) / kC;  // this CTA's tiles
+            const Role ro = role_of<kC>(item_id[s], rank, kTs);
+            if (ro.w < 0) break;
+            const DecItem it = dec_decode(ro.w, p, ro.max_tiles);
+            const int32_t nl = (it.nkt - ro.cr + ro.cc - 1) / ro.cc;  // this CTA's tiles
+            // the CTA that writes the row's tail and runs the selection: the leader of a
+            // shared item, or the CTA that has the item alone
+            const bool owner = !ro.joint || rank == 0;
             __nv_bfloat16 *orow = p.out + ((int64_t)it.g * p.T + it.t) * p.out_stride;
             int32_t zero_from = 0;  // first column of the row to zero-fill
             __nv_bfloat16 *srow = reinterpret_cast<__nv_bfloat16 *>(sgen + kDecOffSel + kSelOffRow);
             const uint32_t srow_leader = kPair ? mapa_shared(sbase + kDecOffSel + kSelOffRow, 0) : 0u;
             SelPre pre{};
-            if (kSel && rank == 0) {
+            if (kSel && owner) {
                 pre = dec_sel_pre(sel, it);
                 // the histograms, and the row's columns past its tensor-memory tiles that
                 // the pooling windows reach (4 * NB <= out_stride)
@@ -1461,7 +1500,7 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                 // the item's tile kC*i + rank, key column col(i)
                 constexpr int kTB = 64 / G;
                 float vb[kTB][G], m[G], l[G];
-                auto col = [&](int32_t i) { return (kC * i + (int32_t)rank) * kBN + key; };
+                auto col = [&](int32_t i) { return (ro.cc * i + ro.cr) * kBN + key; };
                 auto load_batch = [&](int32_t kt0) {
 #pragma unroll
                     for (int b = 0; b < kTB; ++b)
@@ -1488,7 +1527,7 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                 // keys past the tensor-memory tiles (an out_stride below the sequence's key
                 // count): into the statistics only, on CUDA cores
                 const uint8_t *qtile = sgen + s * kDecQSlot;
-                for (int32_t j = it.nkt * kBN + tid; rank == 0 && j < it.vis; j += kDecEpiWarps * 32) {
+                for (int32_t j = it.nkt * kBN + tid; owner && j < it.vis; j += kDecEpiWarps * 32) {
 #pragma unroll
                     for (int h0 = 0; h0 < G; h0 += 8) {
                         float sc[8];
@@ -1498,7 +1537,7 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                     }
                 }
                 dec_reduce<G, true>(m, red, warp, lane);
-                if constexpr (kPair) {  // the pair's max: this CTA's and the peer's
+                if (kPair && ro.joint) {  // the pair's max: this CTA's and the peer's
                     if (tid == 0) {
                         const uint32_t rx = mapa_shared(pbase + kPairX, rank ^ 1u);
 #pragma unroll
@@ -1522,7 +1561,7 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                         }
                     }
                 }
-                for (int32_t j = it.nkt * kBN + tid; rank == 0 && j < it.vis; j += kDecEpiWarps * 32) {
+                for (int32_t j = it.nkt * kBN + tid; owner && j < it.vis; j += kDecEpiWarps * 32) {
 #pragma unroll
                     for (int h0 = 0; h0 < G; h0 += 8) {
                         float sc[8];
@@ -1532,7 +1571,7 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                     }
                 }
                 dec_reduce<G, false>(l, red + (kDecEpiWarps + 1) * 32, warp, lane);
-                if constexpr (kPair) {  // the pair's sum (both halves taken against the pair's max)
+                if (kPair && ro.joint) {  // the pair's sum (both halves taken against the pair's max)
                     if (tid == 0) {
                         const uint32_t rx = mapa_shared(pbase + kPairX + 128, rank ^ 1u);
 #pragma unroll
@@ -1566,13 +1605,13 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                             const __nv_bfloat16 ob = __float2bfloat16_rn(o);
                             if (p.out) orow[j] = ob;
                             if constexpr (kSel) {
-                                if (rank == 0) srow[j] = ob;
+                                if (owner) srow[j] = ob;
                                 else st_cluster_u16(srow_leader + 2 * j, __bfloat16_as_ushort(ob));
                             }
                         }
                     }
                 }
-                if (kPair && kSel && rank != 0) mbar_arrive_remote(mapa_shared(row_full, 0));
+                if (kPair && kSel && !owner) mbar_arrive_remote(mapa_shared(row_full, 0));
                 named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);  // every thread has read item_id[s]
                 tbase += (uint32_t)nl;
                 zero_from = it.nkt * kBN;
@@ -1580,9 +1619,9 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                 named_bar_sync(kDecEpiBarrier, kDecEpiWarps * 32);  // every thread has read item_id[s]
             }
             if (tid == 0) mbar_arrive(item_empty + 8 * s);
-            const bool exchanged = it.active && it.nkt > 0;
-            if (kPair && exchanged) ++xn;
-            if (rank != 0) continue;  // the leader writes the row's tail and runs the selection
+            const bool exchanged = ro.joint && it.active && it.nkt > 0;
+            if (exchanged) ++xn;
+            if (!owner) continue;  // the leader writes the row's tail and runs the selection
             if (kPair && kSel && exchanged) {  // the peer's columns have landed in srow
                 const bool br = !wait_bar<true>(sy, row_full, (xn - 1) & 1, 22);
                 if (named_bar_or(kDecEpiBarrier, kDecEpiWarps * 32, br)) break;
@@ -1666,15 +1705,26 @@ bool use_decode_kernel(int64_t G, int64_t T, int64_t n_seq, int64_t out_stride, 
     return T <= 4 * n_seq;
 }
 
-// Decode items shared by CTA pairs when every pair gets at most one item (items <= SMs/2):
-// then the longest item bounds the kernel, and a pair streams it at about twice the
-// rate of one SM.  With more items, pairs measured slower (two rounds of items where
-// single CTAs need one).  UNUM_DECODE_PAIRS=0 or =1 forces the choice, for testing.
-bool use_pairs(int64_t items) {
+// How the decode kernel spreads items over SMs: the first joint_items items are shared
+// by a CTA pair (a cluster of two streams an item at about twice the rate of one SM),
+// the rest get one CTA each; -1: no pairs.
+//  - items <= SMs/2: every item shared;
+//  - SMs/2 < items <= SMs: the first SMs - items items shared, so all items still start
+//    in one round (shared ones take two SMs, the others one); a caller that orders its
+//    batch longest first gets its longest items shared;
+//  - more items: one CTA per item (pairs measured slower there: sharing costs SM time a
+//    batch of many items needs).
+// UNUM_DECODE_PAIRS=0|1 and UNUM_DECODE_JOINT_ITEMS=n force the choice, for testing.
+int64_t decode_joint_items(int64_t items) {
     const char *env = getenv("UNUM_DECODE_PAIRS");
-    if (env && env[0] == '0') return false;
-    if (env && env[0] == '1') return true;
-    return 2 * items <= unum::sm_count();
+    const char *ji = getenv("UNUM_DECODE_JOINT_ITEMS");
+    const int64_t forced = ji ? (int64_t)atoll(ji) : -1;
+    if (env && env[0] == '0') return -1;
+    if (env && env[0] == '1') return forced >= 0 ? forced : items;
+    const int64_t sms = unum::sm_count();
+    if (2 * items <= sms) return forced >= 0 ? forced : items;
+    if (items <= sms) return forced >= 0 ? forced : sms - items;
+    return -1;
 }
 
 int stage1_run(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, int64_t q_sh,
@@ -1764,7 +1814,8 @@ int stage1_run(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, in
         p.k_st = k_st;
         p.k_sh = k_sh;
         p.force_expiry = force_expiry;
-        const bool pair = use_pairs(T * Hk);
+        p.joint_items = decode_joint_items(T * Hk);
+        const bool pair = p.joint_items >= 0;
         if (sel) {
             if (pair)
                 return G == 16 ? launch_decode<16, true, 2>(mqd, mk, p, *sel, s)
@@ -1816,6 +1867,7 @@ int stage1_run(const void *q, int64_t T, int64_t Hq, int64_t D, int64_t q_st, in
     p.k_st = k_st;
     p.k_sh = k_sh;
     p.force_expiry = force_expiry;
+    p.joint_items = 0;
     switch (G) {
         case 2: return launch_main<2>(mq, mk, mo, p, T, s);
         case 4: return launch_main<4>(mq, mk, mo, p, T, s);
