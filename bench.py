@@ -222,6 +222,39 @@ def make_inputs(seed, device):
     return host
 
 
+def parse_cpulist(text):
+    """CPU ids of a Linux cpulist string ("0-3,8,10-11")."""
+    cpus = set()
+    for part in text.strip().split(","):
+        if not part:
+            continue
+        a, _, b = part.partition("-")
+        cpus.update(range(int(a), int(b or a) + 1))
+    return cpus
+
+
+def bind_to_gpu_numa(dev_index):
+    """Run this process on the CPUs of its GPU's NUMA node (from sysfs, via the GPU's PCI
+    address), so the pinned host buffers it allocates are placed on that node (first
+    touch) and its host-to-device copies stay on the local socket.  Returns what was done,
+    for the JSON line; leaves the affinity unchanged when sysfs does not say."""
+    import torch
+
+    try:
+        pr = torch.cuda.get_device_properties(dev_index)
+        base = f"/sys/bus/pci/devices/{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        with open(base + "/numa_node") as f:
+            node = int(f.read())
+        with open(base + "/local_cpulist") as f:
+            cpus = parse_cpulist(f.read()) & os.sched_getaffinity(0)
+        if node < 0 or not cpus:
+            return {"numa_node": node, "bound": False}
+        os.sched_setaffinity(0, cpus)
+        return {"numa_node": node, "bound": True, "cpus": len(cpus)}
+    except (OSError, ValueError, AttributeError) as e:
+        return {"bound": False, "why": type(e).__name__}
+
+
 # ------------------------------------------------------------------ our arm
 # Per-token work of pooling, top-k and get_block_table, in units of one visible
 # compressed key of stage 1 (both per kv head), from the kernel times at 128k:
@@ -259,6 +292,7 @@ def run_ours(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    host_binding = bind_to_gpu_numa(local)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
     unum_ops_b200.load()
@@ -571,7 +605,8 @@ def run_ours(args):
                     "api": "block_select_streamed (query chunks of 16384 tokens copied while the "
                            "previous chunk computes)",
                     "shards": "kv head x query range, ranges of near-equal host-to-device bytes"
-                              if strong and world > 1 else "as the device step"},
+                              if strong and world > 1 else "as the device step",
+                    "host_binding": host_binding},
             "gpu_launches": (2 + (1 if nrows == L_SEQ else nh)) * args.steps,
             "clocks": clocks,
         }
@@ -783,6 +818,7 @@ def run_decode(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    host_binding = bind_to_gpu_numa(local)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
     unum_ops_b200.load()

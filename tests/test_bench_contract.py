@@ -22,3 +22,13 @@ def test_reference_arm_prints_one_contract_line():
     assert d["impl"] == "reference" and d["value"] > 0 and d["unit"] == "tokens/s"
     assert d["e2e"]["value"] == d["value"] and d["e2e"]["h2d_bytes_per_step"] == 0
     assert {"value", "unit", "cores", "kind", "sample"} <= set(d["cpu_baseline"])
+
+
+def test_cpulist_parser():
+    """bench.py binds each rank to its GPU's NUMA-local CPUs from sysfs cpulists."""
+    sys.path.insert(0, ROOT)
+    import bench
+
+    assert bench.parse_cpulist("0-3,8,10-11\n") == {0, 1, 2, 3, 8, 10, 11}
+    assert bench.parse_cpulist("5") == {5}
+    assert bench.parse_cpulist("") == set()
