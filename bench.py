@@ -331,6 +331,10 @@ def run_ours(args):
     # (an HBM-bound kernel, while the exchange is NVLink traffic); the step ends when both do
     xstream = torch.cuda.Stream(dev) if world > 1 else None
     topk_done = torch.cuda.Event()
+    # --exchange peer: the top-k kernel itself stores the ids into every rank's gathered
+    # buffer over NVLink (symmetric memory), then one bounded cross-GPU signal
+    from unum_ops_b200.sharding import PeerIdExchange
+    xch = PeerIdExchange((HK, L_SEQ, TOPK), dev) if world > 1 and args.exchange == "peer" else None
 
     def step(ev=None):
         """One block-selection pass over this rank's shard: stage 1 with the pooling
@@ -345,7 +349,14 @@ def run_ours(args):
             ws.data_ptr(), ws.numel(), stream.cuda_stream))
         if ev is not None:
             ev[1].record(stream)
-        if nrows == L_SEQ:  # every row: one launch over the heads' rows together
+        if xch is not None:
+            xch.begin()
+            if nrows == L_SEQ:
+                xch.topk(pooled.view(nh * nrows, NB), TOPK, idx.view(nh * nrows, TOPK), g0 * L_SEQ * TOPK)
+            else:
+                for h in range(nh):
+                    xch.topk(pooled[h, ta:tb_], TOPK, idx[h], ((g0 + h) * L_SEQ + ta) * TOPK)
+        elif nrows == L_SEQ:  # every row: one launch over the heads' rows together
             unum_ops_b200._lib.check(L.unum_topk_blocks(
                 pooled.data_ptr(), 1, nh * nrows, NB, NB, TOPK, idx.data_ptr(), stream.cuda_stream))
         else:
@@ -355,7 +366,7 @@ def run_ours(args):
                     stream.cuda_stream))
         if ev is not None:
             ev[2].record(stream)
-        if world > 1:
+        if world > 1 and xch is None:
             topk_done.record(stream)
             xstream.wait_event(topk_done)
             with torch.cuda.stream(xstream):
@@ -368,7 +379,13 @@ def run_ours(args):
                               head_offset=g0, out=slots)
         if ev is not None:
             ev[3].record(stream)
-        if world > 1:
+        if xch is not None:
+            if ev is not None:
+                ev[5].record(stream)
+            xch.finish(full_idx)
+            if ev is not None:
+                ev[6].record(stream)
+        elif world > 1:
             stream.wait_stream(xstream)
         if ev is not None:
             ev[4].record(stream)
@@ -398,6 +415,8 @@ def run_ours(args):
     wall1 = time.time()
     clk.stop()
     total_ms = t_start.elapsed_time(t_end)
+    if xch is not None:
+        xch.check()
     if world > 1:
         # the overlapped exchange delivered the ids: this rank's own shard is in place, and
         # every rank holds the same gathered tensor
@@ -555,9 +574,14 @@ def run_ours(args):
             kernels[kname] = {"ms": mean[kname], "gbs": gbs, "frac": gbs / hbm, "bound": "hbm"}
         if world > 1:
             kernels["topk_idx_gather"] = {"ms": mean["gather"], "bytes": full_idx.numel() * 2,
-                                          "how": "NCCL send/recv of each rank's exact shard, int16 "
-                                                 "on the wire, widened to int32 once; on a side "
-                                                 "stream, overlapping get_block_table",
+                                          "how": ("fused into the top-k kernel: int16 ids stored into "
+                                                  "every rank's gathered buffer over NVLink (symmetric "
+                                                  "memory), then a bounded cross-GPU signal and the "
+                                                  "int32 widening (ms = signal + widening)")
+                                                 if xch is not None else
+                                                 ("NCCL send/recv of each rank's exact shard, int16 "
+                                                  "on the wire, widened to int32 once; on a side "
+                                                  "stream, overlapping get_block_table"),
                                           "after_topk_ms": mean["tail"]}
         cpu = None
         if args.cpu_sample > 0 and world == 1:
@@ -966,6 +990,9 @@ def main():
     ap.add_argument("--decode-batch", type=int, default=512,
                     help="decode batch (config 4: 512 sequences); the prefill line also carries "
                          "its measurement under 'decode' (0: skip)")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="N>1 top-k id exchange: fused into the top-k kernel over NVLink (peer), "
+                         "or NCCL send/recv after it (nccl)")
     ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
                     help="N>1: strong = one sequence sharded by kv head x query range "
                          "(config 3); weak = every rank its own sequence")

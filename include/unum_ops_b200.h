@@ -131,6 +131,35 @@ int unum_topk_blocks(const void *scores, int dtype, int64_t rows, int64_t NB,
                      int64_t row_stride, int64_t K, int32_t *out, void *stream);
 
 /*
+ * topk_blocks_to_peers — topk_blocks whose rows also go, narrowed to int16, into the
+ * buffers of every rank of a multi-GPU job (the top-k id exchange fused into the
+ * kernel: plain stores over NVLink while the kernel selects, no separate collective).
+ * No reference counterpart.
+ *   peer_bufs  n_peers (1..8) int16 buffers, each mapped into this device's address
+ *              space (e.g. the peers' pointers of a symmetric-memory allocation; this
+ *              rank's own buffer among them); row r is stored at
+ *              peer_bufs[i] + peer_offset + r*K for every i
+ * Ids are below NB <= 32768, so int16 holds them (-1 stays -1).  K and peer_offset
+ * must be even, the buffers 4-byte aligned.  The stores are complete on the peers
+ * once unum_peer_signal_wait has passed on every rank.
+ */
+int unum_topk_blocks_to_peers(const void *scores, int dtype, int64_t rows, int64_t NB,
+                              int64_t row_stride, int64_t K, int32_t *out, void *const *peer_bufs,
+                              int32_t n_peers, int64_t peer_offset, void *stream);
+
+/*
+ * peer_signal_wait — cross-GPU step signal for such exchanges.  No reference
+ * counterpart.  signal_bufs[i] = rank i's array of n_ranks int32 words (peer-mapped,
+ * zeroed before the first step); epoch increases by one per step.  Each rank announces
+ * the epoch to every peer (after a system-scope fence over its earlier stores) and
+ * waits, on the stream, until every peer has announced it.  The wait is bounded (about
+ * one second per peer); on expiry *status (if not NULL) becomes 40 and the kernel
+ * returns, so a missing peer yields an error status rather than a hung GPU.
+ */
+int unum_peer_signal_wait(int32_t *const *signal_bufs, int32_t n_ranks, int32_t rank, int32_t epoch,
+                          int32_t *status, void *stream);
+
+/*
  * infllmv2_attn_stage1 — compressed-key GQA scores, softmax per head, summed
  * over each head group.  Replaces infllmv2_attn_stage1_triton_v2
  * (infllmv2_attn_stage1_triton_v2.py:153-228; kernel :19-150).

@@ -36,6 +36,8 @@ SIGNATURES = {
     "unum_max_pooling_1d_varlen": ([_p, _int, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64,
                                     _i64, _i64, _i64, _p, _p], _int),
     "unum_topk_blocks": ([_p, _int, _i64, _i64, _i64, _i64, _p, _p], _int),
+    "unum_topk_blocks_to_peers": ([_p, _int, _i64, _i64, _i64, _i64, _p, _p, _i32, _i64, _p], _int),
+    "unum_peer_signal_wait": ([_p, _i32, _i32, _i32, _p, _p], _int),
     "unum_compress_keys": ([_p, _i64, _i64, _i64, _i64, _i64, _p, _p, _i64, _i64, _i64, _i64, _p, _p],
                            _int),
     "unum_stage1_workspace_size": ([_i64], ctypes.c_size_t),

@@ -450,6 +450,15 @@ __device__ __forceinline__ void load8_keys(const T *src, int32_t i0, int32_t NB,
     }
 }
 
+// Buffers on other GPUs (peer-mapped into this device's address space) that also receive
+// every row's ids, narrowed to int16: row r goes to p[i] + off + r*K for each i < n.
+constexpr int kMaxPeers = 8;
+struct Peers {
+    int16_t *p[kMaxPeers];
+    int32_t n;
+    int64_t off;
+};
+
 // Score value whose key is k (inverse of KeyOf<T>::key for non-excluded keys).
 template <typename T> __device__ __forceinline__ float key_value(uint32_t k);
 template <> __device__ __forceinline__ float key_value<float>(uint32_t k) {
@@ -475,7 +484,7 @@ template <> __device__ __forceinline__ float key_value<float>(uint32_t k) {
 template <typename T, int kMaxW>  // kMaxW: 2 for rows of at most 2048 blocks, else 4
 __global__ void __launch_bounds__(kWarps * 32, sizeof(T) == 2 ? kMinBlocks16 : 1)  // 16-bit: 7 blocks, <= 72 registers
 topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_stride, int32_t K,
-            bool vec_ok, int64_t rows_per_warp, int32_t *__restrict__ out) {
+            bool vec_ok, int64_t rows_per_warp, int32_t *__restrict__ out, const __grid_constant__ Peers peers) {
     using Key = typename KeyOf<T>::K;
     constexpr int PASSES = KeyOf<T>::kPasses;
     extern __shared__ __align__(16) uint8_t smem[];
@@ -679,12 +688,22 @@ topk_kernel(const T *__restrict__ scores, int64_t rows, int32_t NB, int64_t row_
         }
         tau_prev = take_all ? 0u : prefix;
         __syncwarp();
+        if (peers.n > 0) {
+            // the row's ids (written by the lanes of this warp just above) as int16 pairs into
+            // every peer's buffer: plain stores over NVLink, 2*K bytes per row per peer
+            for (int32_t i = 2 * lane; i < K; i += 64) {
+                const uint32_t pk = (uint32_t)(uint16_t)orow[i] | ((uint32_t)(uint16_t)orow[i + 1] << 16);
+                const int64_t e = peers.off + row * K + i;
+                for (int j = 0; j < peers.n; ++j) *reinterpret_cast<uint32_t *>(peers.p[j] + e) = pk;
+            }
+            __syncwarp();
+        }
     }
 }
 
 template <typename T>
 int launch_topk(const void *scores, int64_t rows, int64_t NB, int64_t row_stride, int64_t K,
-                int32_t *out, cudaStream_t s) {
+                int32_t *out, cudaStream_t s, const Peers &peers) {
     using Key = typename KeyOf<T>::K;
     const size_t smem = (size_t)kWarps * warp_smem_bytes<Key>(NB);
     const int64_t NBp = (NB + 255) / 256 * 256;
@@ -700,15 +719,15 @@ int launch_topk(const void *scores, int64_t rows, int64_t NB, int64_t row_stride
     const int64_t rows_per_warp = (rows + nwarps - 1) / nwarps;
     const bool vec_ok = unum::aligned16(scores) && ((row_stride * (int64_t)sizeof(T)) % 16 == 0);
     kern<<<grid, kWarps * 32, smem, s>>>((const T *)scores, rows, (int32_t)NB, row_stride, (int32_t)K,
-                                         vec_ok, rows_per_warp, out);
+                                         vec_ok, rows_per_warp, out, peers);
     return unum::check_launch("topk_kernel");
 }
 
 }  // namespace
 
-extern "C" int unum_topk_blocks(const void *scores, int dtype, int64_t rows, int64_t NB,
-                                int64_t row_stride, int64_t K, int32_t *out, void *stream) {
-    unum::clear_error();
+namespace {
+int topk_run(const void *scores, int dtype, int64_t rows, int64_t NB, int64_t row_stride, int64_t K,
+             int32_t *out, void *stream, const Peers &peers) {
     UNUM_CHECK_ARG(rows >= 0 && NB >= 0 && K >= 0, "negative size");
     if (rows == 0 || K == 0) return UNUM_OK;
     UNUM_CHECK_ARG(out != nullptr, "null output");
@@ -721,11 +740,40 @@ extern "C" int unum_topk_blocks(const void *scores, int dtype, int64_t rows, int
         return UNUM_OK;
     }
     switch (dtype) {
-        case UNUM_DTYPE_F32: return launch_topk<float>(scores, rows, NB, row_stride, K, out, s);
-        case UNUM_DTYPE_BF16: return launch_topk<__nv_bfloat16>(scores, rows, NB, row_stride, K, out, s);
-        case UNUM_DTYPE_F16: return launch_topk<__half>(scores, rows, NB, row_stride, K, out, s);
+        case UNUM_DTYPE_F32: return launch_topk<float>(scores, rows, NB, row_stride, K, out, s, peers);
+        case UNUM_DTYPE_BF16: return launch_topk<__nv_bfloat16>(scores, rows, NB, row_stride, K, out, s, peers);
+        case UNUM_DTYPE_F16: return launch_topk<__half>(scores, rows, NB, row_stride, K, out, s, peers);
         default:
             unum::set_error("unsupported dtype %d", dtype);
             return UNUM_ERR_UNSUPPORTED;
     }
+}
+}  // namespace
+
+extern "C" int unum_topk_blocks(const void *scores, int dtype, int64_t rows, int64_t NB,
+                                int64_t row_stride, int64_t K, int32_t *out, void *stream) {
+    unum::clear_error();
+    Peers none{};
+    return topk_run(scores, dtype, rows, NB, row_stride, K, out, stream, none);
+}
+
+extern "C" int unum_topk_blocks_to_peers(const void *scores, int dtype, int64_t rows, int64_t NB,
+                                         int64_t row_stride, int64_t K, int32_t *out,
+                                         void *const *peer_bufs, int32_t n_peers, int64_t peer_offset,
+                                         void *stream) {
+    unum::clear_error();
+    UNUM_CHECK_ARG(n_peers >= 1 && n_peers <= kMaxPeers && peer_bufs != nullptr,
+                   "1 to %d peer buffers needed", kMaxPeers);
+    UNUM_CHECK_ARG(NB >= 1 && NB <= 32768, "ids travel as int16: 1 <= NB <= 32768 (got %lld)", (long long)NB);
+    UNUM_CHECK_ARG(K % 2 == 0 && peer_offset >= 0 && peer_offset % 2 == 0,
+                   "K and peer_offset must be even (ids travel in 4-byte pairs)");
+    Peers peers{};
+    peers.n = n_peers;
+    peers.off = peer_offset;
+    for (int i = 0; i < n_peers; ++i) {
+        UNUM_CHECK_ARG(peer_bufs[i] != nullptr && ((uintptr_t)peer_bufs[i] & 3) == 0,
+                       "peer buffer %d null or not 4-byte aligned", i);
+        peers.p[i] = (int16_t *)peer_bufs[i];
+    }
+    return topk_run(scores, dtype, rows, NB, row_stride, K, out, stream, peers);
 }

@@ -138,3 +138,91 @@ def exchange_shards(local, full, shards, rank, group=None, wire=None):
     if wire is not None:
         full.copy_(wire)
     return full
+
+
+def _rendezvous(t, group):
+    """Symmetric-memory handle of ``t`` over ``group`` (peer pointers by rank)."""
+    import torch.distributed._symmetric_memory as symm
+
+    try:
+        return symm.rendezvous(t, group)
+    except RuntimeError:
+        symm.enable_symm_mem_for_group(group.group_name)
+        return symm.rendezvous(t, group)
+
+
+class PeerIdExchange:
+    """The top-k id exchange fused into the top-k kernel.
+
+    Every rank's top-k kernel (``unum_topk_blocks_to_peers``) stores each row's ids,
+    narrowed to int16, straight into the gathered ``[Hk, T, K]`` buffer of every rank
+    over NVLink while it selects; then ``finish`` runs the bounded cross-GPU signal
+    (``unum_peer_signal_wait``) and widens this rank's buffer into the int32 result.
+    There is no separate collective.  The buffers are symmetric memory (the same
+    allocation on every rank, peer-mapped) and alternate by step, so a rank that starts
+    the next step early never writes into a buffer a slower rank is still reading.
+
+    Per step: ``begin()``, then ``topk(...)`` for each of this rank's launches (with the
+    element offset of its rows in the gathered buffer), then ``finish(full)``.
+    """
+
+    def __init__(self, shape, device, group=None):
+        import ctypes
+
+        import torch.distributed as dist
+
+        from . import _lib
+
+        self.group = group if group is not None else dist.group.WORLD
+        self.rank = dist.get_rank(self.group)
+        self.world = dist.get_world_size(self.group)
+        if self.world > 8:
+            raise ValueError("at most 8 ranks")
+        import torch.distributed._symmetric_memory as symm
+
+        self.wire = [symm.empty(*shape, dtype=torch.int16, device=device) for _ in range(2)]
+        self.sig = symm.empty(self.world, dtype=torch.int32, device=device)
+        self.sig.zero_()
+        hw = [_rendezvous(w, self.group) for w in self.wire]
+        hs = _rendezvous(self.sig, self.group)
+        self.ptrs = [(ctypes.c_void_p * self.world)(*h.buffer_ptrs) for h in hw]
+        self.sig_ptrs = (ctypes.c_void_p * self.world)(*hs.buffer_ptrs)
+        self._handles = hw + [hs]  # keep the mappings alive
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self.device = device
+        self.epoch = 0
+        self._lib = _lib
+        torch.cuda.synchronize(device)
+        dist.barrier(self.group)  # every signal array is zero before anyone announces
+
+    def begin(self):
+        self.epoch += 1
+
+    def topk(self, pooled_rows, K, out, offset):
+        """Top-K of ``pooled_rows`` [rows, NB] (16-bit or fp32) into ``out`` [rows, K]
+        int32 on this rank, and the same ids as int16 at element ``offset`` of every
+        rank's gathered buffer."""
+        L = self._lib.load()
+        rows, NB = pooled_rows.shape
+        with torch.cuda.device(self.device):
+            rc = L.unum_topk_blocks_to_peers(
+                pooled_rows.data_ptr(), self._lib.DTYPE_CODES[pooled_rows.dtype], rows, NB,
+                pooled_rows.stride(0), K, out.data_ptr(), self.ptrs[self.epoch & 1], self.world,
+                int(offset), self._lib.stream_ptr(self.device))
+        self._lib.check(rc)
+
+    def finish(self, full):
+        """Wait (on the stream) until every rank's stores of this step have landed, then
+        widen the gathered ids into ``full`` (int32, the buffer's shape)."""
+        L = self._lib.load()
+        with torch.cuda.device(self.device):
+            rc = L.unum_peer_signal_wait(self.sig_ptrs, self.world, self.rank, self.epoch,
+                                         self.status.data_ptr(), self._lib.stream_ptr(self.device))
+        self._lib.check(rc)
+        full.copy_(self.wire[self.epoch & 1])
+        return full
+
+    def check(self):
+        """Raise if a signal wait gave up (a peer did not announce within about a second)."""
+        if int(self.status.item()) != 0:
+            raise RuntimeError(f"peer signal wait expired (status {int(self.status.item())})")
