@@ -872,7 +872,11 @@ constexpr uint32_t kPairInbox = 0;                        // int64 [kDecSlots]
 constexpr uint32_t kPairX = kPairInbox + 8 * kDecSlots;   // float [2][32]: peer's max, sum
 constexpr uint32_t kPairBars = kPairX + 2 * 32 * 4;       // item_in[slots], peer_empty[slots], x_full[2], row_full
 constexpr uint32_t kPairBytes = kPairBars + (2 * kDecSlots + 3) * 8;
-constexpr uint32_t kDecOffSel = (kDecOffPair + kPairBytes + 127) & ~127u;
+// each item slot's decoded item, written by the producer (the MMA warp and the epilogue
+// read it instead of repeating the sequence search on their critical paths)
+constexpr uint32_t kDecItemBytes = 64;
+constexpr uint32_t kDecOffItems = (kDecOffPair + kPairBytes + 15) & ~15u;
+constexpr uint32_t kDecOffSel = (kDecOffItems + kDecSlots * kDecItemBytes + 127) & ~127u;
 constexpr uint32_t kDecSmemBytesSel = kDecOffSel + kSelBytes + 1024;
 constexpr uint32_t kDecSmemBytesPair = kDecOffSel + 1024;
 static_assert(kDecSmemBytesSel <= 232448, "exceeds the 227 KB of shared memory a CTA may use");
@@ -1304,6 +1308,8 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
     Sync sy;
     sy.abort = abort_flag;
     sy.status = p.ws;
+    DecItem *slot_item = reinterpret_cast<DecItem *>(sgen + kDecOffItems);  // [kDecSlots]
+    static_assert(sizeof(DecItem) <= kDecItemBytes, "decoded item larger than its slot");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr bool kPair = kC == 2;
     const uint32_t rank = kPair ? cluster_ctarank() : 0u;
@@ -1392,6 +1398,7 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                 const Role ro = role_of<kC>(v, rank, kTs);
                 const int64_t w = ro.w;
                 const DecItem it = w >= 0 ? dec_decode(w, p, ro.max_tiles) : DecItem{};
+                slot_item[s] = it;  // published to the MMA warp and the epilogue by item_full
                 const int32_t nl = (it.nkt - ro.cr + ro.cc - 1) / ro.cc;  // this CTA's tiles
                 item_id[s] = v;
                 if (w >= 0 && nl > 0) {
@@ -1425,7 +1432,7 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                 if (!wait_bar(sy, item_full + 8 * s, sph, 13)) break;
                 const Role ro = role_of<kC>(item_id[s], rank, kTs);
                 if (ro.w < 0) break;
-                const DecItem it = dec_decode(ro.w, p, ro.max_tiles);
+                const DecItem it = slot_item[s];
                 const int32_t nl = (it.nkt - ro.cr + ro.cc - 1) / ro.cc;
                 if (nl <= 0) {
                     mbar_arrive(tmem_full + 8 * s);  // one phase per use of the slot
@@ -1473,7 +1480,7 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
             if (named_bar_or(kDecEpiBarrier, kDecEpiWarps * 32, bad)) break;  // gave up: all leave
             const Role ro = role_of<kC>(item_id[s], rank, kTs);
             if (ro.w < 0) break;
-            const DecItem it = dec_decode(ro.w, p, ro.max_tiles);
+            const DecItem it = slot_item[s];
             const int32_t nl = (it.nkt - ro.cr + ro.cc - 1) / ro.cc;  // this CTA's tiles
             // the CTA that writes the row's tail and runs the selection: the leader of a
             // shared item, or the CTA that has the item alone
