@@ -874,7 +874,7 @@ constexpr uint32_t kPairBars = kPairX + 2 * 32 * 4;       // item_in[slots], pee
 constexpr uint32_t kPairBytes = kPairBars + (2 * kDecSlots + 3) * 8;
 // each item slot's decoded item, written by the producer (the MMA warp and the epilogue
 // read it instead of repeating the sequence search on their critical paths)
-constexpr uint32_t kDecItemBytes = 64;
+constexpr uint32_t kDecItemBytes = 96;  // the decoded item, then (fused selection) its SelPre
 constexpr uint32_t kDecOffItems = (kDecOffPair + kPairBytes + 15) & ~15u;
 constexpr uint32_t kDecOffSel = (kDecOffItems + kDecSlots * kDecItemBytes + 127) & ~127u;
 constexpr uint32_t kDecSmemBytesSel = kDecOffSel + kSelBytes + 1024;
@@ -1121,8 +1121,8 @@ __device__ __forceinline__ Role role_of(int64_t v, uint32_t rank, int32_t tmem_t
     return r;
 }
 
-// Per-token values the selection needs from global memory, loaded when the epilogue
-// takes the item so that their latency hides behind its three passes.
+// Per-token values the selection needs from global memory, loaded by the producer with
+// the item and handed over in its slot, so the epilogue never waits on them.
 struct SelPre {
     int32_t k_len;   // the pooling's key count: compressed keys + cache_lens[b]
     int32_t off_bq;  // the token's local block
@@ -1309,7 +1309,8 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
     sy.abort = abort_flag;
     sy.status = p.ws;
     DecItem *slot_item = reinterpret_cast<DecItem *>(sgen + kDecOffItems);  // [kDecSlots]
-    static_assert(sizeof(DecItem) <= kDecItemBytes, "decoded item larger than its slot");
+    SelPre *slot_pre = reinterpret_cast<SelPre *>(sgen + kDecOffItems + kDecSlots * 64);  // [kDecSlots]
+    static_assert(sizeof(DecItem) <= 64 && sizeof(SelPre) <= 32, "decoded item larger than its slot");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr bool kPair = kC == 2;
     const uint32_t rank = kPair ? cluster_ctarank() : 0u;
@@ -1399,6 +1400,8 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
                 const int64_t w = ro.w;
                 const DecItem it = w >= 0 ? dec_decode(w, p, ro.max_tiles) : DecItem{};
                 slot_item[s] = it;  // published to the MMA warp and the epilogue by item_full
+                if constexpr (kSel)
+                    if (w >= 0) slot_pre[s] = dec_sel_pre(sel, it);
                 const int32_t nl = (it.nkt - ro.cr + ro.cc - 1) / ro.cc;  // this CTA's tiles
                 item_id[s] = v;
                 if (w >= 0 && nl > 0) {
@@ -1491,7 +1494,7 @@ stage1_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_const
             const uint32_t srow_leader = kPair ? mapa_shared(sbase + kDecOffSel + kSelOffRow, 0) : 0u;
             SelPre pre{};
             if (kSel && owner) {
-                pre = dec_sel_pre(sel, it);
+                pre = slot_pre[s];
                 // the histograms, and the row's columns past its tensor-memory tiles that
                 // the pooling windows reach (4 * NB <= out_stride)
                 int32_t *hist = reinterpret_cast<int32_t *>(sgen + kDecOffSel + kSelOffHist);
