@@ -298,6 +298,9 @@ def run_ours(args):
     unum_ops_b200.load()
     L = unum_ops_b200.load()
     strong = args.scaling == "strong"
+    # the top-k ids are gathered across ranks only when they share one sequence (strong
+    # scaling); with weak scaling every rank's result is its own
+    gather = world > 1 and strong
     g0, nh, ta, tb_ = shard_of(world, rank, strong)
     nrows = tb_ - ta
     G = HQ // HK
@@ -329,12 +332,12 @@ def run_ours(args):
 
     # the exchange runs on a side stream once top-k is done, overlapping get_block_table
     # (an HBM-bound kernel, while the exchange is NVLink traffic); the step ends when both do
-    xstream = torch.cuda.Stream(dev) if world > 1 else None
+    xstream = torch.cuda.Stream(dev) if gather else None
     topk_done = torch.cuda.Event()
     # --exchange peer: the top-k kernel itself stores the ids into every rank's gathered
     # buffer over NVLink (symmetric memory), then one bounded cross-GPU signal
     from unum_ops_b200.sharding import PeerIdExchange
-    xch = PeerIdExchange((HK, L_SEQ, TOPK), dev) if world > 1 and args.exchange == "peer" else None
+    xch = PeerIdExchange((HK, L_SEQ, TOPK), dev) if gather and args.exchange == "peer" else None
 
     def step(ev=None):
         """One block-selection pass over this rank's shard: stage 1 with the pooling
@@ -366,7 +369,7 @@ def run_ours(args):
                     stream.cuda_stream))
         if ev is not None:
             ev[2].record(stream)
-        if world > 1 and xch is None:
+        if gather and xch is None:
             topk_done.record(stream)
             xstream.wait_event(topk_done)
             with torch.cuda.stream(xstream):
@@ -385,7 +388,7 @@ def run_ours(args):
             xch.finish(full_idx)
             if ev is not None:
                 ev[6].record(stream)
-        elif world > 1:
+        elif gather:
             stream.wait_stream(xstream)
         if ev is not None:
             ev[4].record(stream)
@@ -417,8 +420,8 @@ def run_ours(args):
     total_ms = t_start.elapsed_time(t_end)
     if xch is not None:
         xch.check()
-    if world > 1:
-        # the overlapped exchange delivered the ids: this rank's own shard is in place, and
+    if gather:
+        # the exchange delivered the ids: this rank's own shard is in place, and
         # every rank holds the same gathered tensor
         torch.cuda.synchronize(dev)
         assert torch.equal(full_idx[g0:g0 + nh, ta:tb_], idx), "own top-k shard missing after the exchange"
@@ -433,7 +436,7 @@ def run_ours(args):
         per["stage1"].append(e[0].elapsed_time(e[1]))
         per["topk"].append(e[1].elapsed_time(e[2]))
         per["get_block_table"].append(e[2].elapsed_time(e[3]))
-        if world > 1:
+        if gather:
             per["gather"].append(e[5].elapsed_time(e[6]))
             per["tail"].append(e[2].elapsed_time(e[4]))
     ms_step = total_ms / args.steps
@@ -572,7 +575,7 @@ def run_ours(args):
         for kname in ("topk", "get_block_table"):
             gbs = ab[kname] / (mean[kname] * 1e-3) / 1e9
             kernels[kname] = {"ms": mean[kname], "gbs": gbs, "frac": gbs / hbm, "bound": "hbm"}
-        if world > 1:
+        if gather:
             kernels["topk_idx_gather"] = {"ms": mean["gather"], "bytes": full_idx.numel() * 2,
                                           "how": ("fused into the top-k kernel: int16 ids stored into "
                                                   "every rank's gathered buffer over NVLink (symmetric "
