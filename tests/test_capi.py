@@ -88,3 +88,31 @@ def test_public_names_match_reference():
     assert set(ske.__all__) == {"get_block_table_ref_torch", "get_block_table_ref_triton",
                                 "get_block_table_ref_triton_v2", "get_block_table_ref_triton_v3",
                                 "get_block_table_v2", "get_block_table_v3"}
+
+
+def test_decode_fusion_routing():
+    """block_select takes the one-launch decode path exactly for the shapes the fused
+    kernel supports: a head group of 16 or 32, head_dim 128, 64-token blocks of stride-16
+    compressed keys, at most 4 query tokens per sequence, each row within tensor memory
+    (W <= 128*512/G) and every pooling window inside the row (4*NB <= W)."""
+    import torch
+
+    from unum_ops_b200.block_select import _decode_fusable
+
+    def case(T=8, hq=32, hk=2, d=128, n_seq=8, tk=100, max_k=1000, ctx=16000, topk=64, bs=64, st=16):
+        q = torch.empty(T, hq, d)
+        k = torch.empty(tk, hk, d)
+        cu_q = torch.zeros(n_seq + 1, dtype=torch.int32)
+        return _decode_fusable(q, k, cu_q, max_k, ctx, topk, bs, st)
+
+    assert case()                               # W = 1024, NB = 250: 4*NB <= W
+    assert case(hq=64, max_k=2000, ctx=32000)   # G = 32: W = 2048 is the largest row
+    assert not case(hq=64, max_k=2100, ctx=32000)  # W = 2176 > 128*512/32
+    assert not case(hq=16)                      # G = 8
+    assert not case(d=64)
+    assert not case(T=40, n_seq=8)              # 5 query tokens per sequence: prefill-like
+    assert not case(ctx=17000)                  # NB = 266: a window past the 1024-wide row
+    assert not case(tk=0)
+    assert not case(topk=1025)
+    assert not case(bs=32)
+    assert not case(T=0)
