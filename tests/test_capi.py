@@ -38,7 +38,7 @@ def test_binding_covers_header():
 
 
 def test_abi_and_workspace(lib):
-    assert lib.unum_abi_version() == 101
+    assert lib.unum_abi_version() == 102
     assert lib.unum_stage1_workspace_size(0) >= 20
     assert lib.unum_stage1_workspace_size(1000) >= 4 * 1005
     assert lib.unum_stage1_workspace_size(1000) % 16 == 0

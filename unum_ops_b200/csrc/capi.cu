@@ -19,4 +19,4 @@ void clear_error() { g_err[0] = 0; }
 
 extern "C" const char *unum_last_error(void) { return unum::g_err; }
 
-extern "C" int unum_abi_version(void) { return 101; }
+extern "C" int unum_abi_version(void) { return 102; }
